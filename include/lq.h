@@ -1,0 +1,137 @@
+/*
+ * lq — C ABI of the B200-native (sm_100a) MLX affine group-quantized matmul path.
+ *
+ * Plain pointers and sizes only. Every pointer is device memory on the current CUDA device
+ * unless stated; `stream` is a cudaStream_t passed as void* (NULL = the legacy default stream).
+ * Nothing here allocates device memory: outputs are caller-allocated, as MLX allocates them for
+ * the reference's kernels. Every entry point returns LQ_OK or an LQ_E_* code and never aborts.
+ *
+ * Weight format (MLX affine, the format every reference kernel consumes; locals/kernels.py:12-13,
+ * locals/qmv_multi.py:23-29, locals/moe.py:181-204): w (N, K*bits/32) uint32, code i of word j is
+ * K index (32/bits)*j + i at bits bits*i (low bits first); scales and biases (N, K/group) in the
+ * activation dtype; dequantized weight = scale * q + bias.
+ */
+#ifndef LQ_H_
+#define LQ_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LQ_OK 0
+#define LQ_E_ARG 1          /* null pointer, bad enum value */
+#define LQ_E_SHAPE 2        /* shape outside what the kernels accept */
+#define LQ_E_ALIGN 3        /* pointer or row stride not aligned as the kernels need */
+#define LQ_E_UNSUPPORTED 4  /* bits / group size / dtype combination not built */
+#define LQ_E_CUDA 5         /* a CUDA runtime call failed (see lq_last_cuda_error) */
+#define LQ_E_DEVICE 6       /* the current device is not an sm_100 GPU */
+
+#define LQ_F16 0
+#define LQ_BF16 1
+#define LQ_F32 2
+
+/* Kernel families, the analogue of the reference's tuning choices (locals/kernels.py:136-144). */
+#define LQ_FAM_AUTO 0   /* pick by shape (M <= 64: QMV, else TC) */
+#define LQ_FAM_QMV 1    /* decode: TMA-staged packed weights, register dequant, mma.sync; p = {MT, R, KS, NS} */
+#define LQ_FAM_TC 2     /* prefill: dequant tiles into shared memory, tcgen05.mma into TMEM */
+
+typedef struct lq_cfg {
+    int family;  /* LQ_FAM_* */
+    int p[7];    /* family parameters, 0 = choose */
+} lq_cfg;
+
+/* y (M, N) = x (M, K) . dequant(w)^T, fp32 accumulation, y in the activation dtype.
+ * Replaces the reference's quantized-linear launcher contract `_launcher(choice, M, K, N, dtype)
+ * -> f(x, w, scales, biases) -> y` (locals/kernels.py:516-576) and `mx.quantized_matmul(x, w,
+ * scales, biases, transpose=True, group_size=64, bits)` (locals/kernels.py:574,1004,1192).
+ * dtype: LQ_F16 / LQ_BF16 for x, scales, biases and y. bits 4 or 8, group_size 64. */
+int lq_qmm(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int M, int N, int K,
+           int bits, int group_size, int dtype, const lq_cfg* cfg, void* stream);
+
+/* Fused projection with its output split along N (the fused q/k/v projection): columns
+ * [0, widths[0]) of x . dequant(w)^T go to outs[0] (M, widths[0]), the next widths[1] to outs[1],
+ * ... (nout <= 3, sum of widths = N). Replaces fuse._concat_quantized + FusedAttention's reshape
+ * and split (locals/fuse.py:28-63). */
+int lq_qmm_split(const void* x, const uint32_t* w, const void* scales, const void* biases, int nout, void* const* outs,
+                 const int* widths, int M, int N, int K, int bits, int group_size, int dtype, const lq_cfg* cfg,
+                 void* stream);
+
+/* h (M, I) = swiglu(x . gate^T, x . up^T) with the rounding points of locals/moe.py:284-289 (each
+ * projection rounded to the activation dtype, then sigmoid, g*sig, act*u each rounded). gate and
+ * up are (I, K) quantized matrices; for a concatenated gate||up (locals/fuse.py:160-199) pass the
+ * same arrays offset by I rows. Replaces FusedMLP's gate_up_proj + swiglu (locals/fuse.py:161-164). */
+int lq_qmm_glu(const void* x, const uint32_t* w_gate, const void* s_gate, const void* b_gate, const uint32_t* w_up,
+               const void* s_up, const void* b_up, void* h, int M, int I, int K, int bits, int group_size, int dtype,
+               const lq_cfg* cfg, void* stream);
+
+/* MLX affine quantization (mx.quantize(w, group_size, bits), as called in the reference's tests,
+ * e.g. tests/test_kernel_patching.py:163): w (N, K) in w_dtype (LQ_F32/LQ_F16/LQ_BF16) ->
+ * wq (N, K*bits/32) uint32, scales and biases (N, K/group_size) in sb_dtype. */
+int lq_quantize(const void* w, int w_dtype, int N, int K, int bits, int group_size, uint32_t* wq, void* scales,
+                void* biases, int sb_dtype, void* stream);
+
+/* mx.dequantize (locals/kernels.py:1007,1024): w_out (N, K) in dtype = scale * q + bias rounded
+ * to dtype (scales/biases in dtype). */
+int lq_dequantize(const uint32_t* wq, const void* scales, const void* biases, int N, int K, int bits, int group_size,
+                  int dtype, void* w_out, void* stream);
+
+/* Router logits in float32: logits (T, E) = float(x) (T, D) . float(w)^T (E, D); x and w may be
+ * f16/bf16 of different dtypes. Replaces moe.router / router_logits (locals/moe.py:118-139). */
+int lq_router_logits(const void* x, int x_dtype, const void* w, int w_dtype, float* logits, int T, int E, int D,
+                     void* stream);
+
+/* Top-k routing of float32 logits (T, E): mode 0 = softmax over E then the k largest, mode 1 =
+ * sigmoid (NaN -> 0) then the k largest (locals/moe.py:36-82,145-165); ties go to the lower expert
+ * index; weights renormalised to sum 1. inds (T, k) uint32 in descending score order, weights
+ * (T, k) float32. E <= 1024, k <= 32. */
+int lq_route_topk(const float* logits, int T, int E, int k, int mode, uint32_t* inds, float* weights, void* stream);
+
+/* Counting sort of P expert ids (locals/moe_kernel.py:28-66,191-197): order (P) = pair ids grouped
+ * by ascending expert (ascending pair id within an expert), starts (min(E,P)+1), experts (min(E,P)),
+ * nseg (1) and, if pos != NULL, pos (P) = the inverse of order. All int32 device arrays. E <= 8192. */
+int lq_moe_group(const uint32_t* inds, int P, int E, int32_t* order, int32_t* starts, int32_t* experts, int32_t* nseg,
+                 int32_t* pos, void* stream);
+
+/* xs (P, D) = x[order[j] / k] for j < P: the tokens of the pairs in expert order (16-bit x, D % 8 == 0). */
+int lq_moe_gather(const void* x, const int32_t* order, int P, int k, int D, void* xs, void* stream);
+
+/* Grouped expert projections (locals/moe_kernel.py:68-155,206-239; mx.gather_qmm of mlx-lm's SwitchGLU,
+ * locals/moe_kernel.py:279): segment s of lq_moe_group covers rows [starts[s], starts[s+1]) of the
+ * pair-ordered xs (P, K) and uses expert experts[s]; each used expert's weights are read once for all
+ * its rows (a segment longer than 64 rows streams them once per 64).
+ * glu != 0: out (P, N) = swiglu(xs . gate_e^T, xs . up_e^T) (rounding of locals/moe.py:284-289);
+ *           gate = (w0, s0, b0), up = (w1, s1, b1), each stacked (E, N, K*bits/32) / (E, N, K/group).
+ * glu == 0: out (P, N) = xs . w0_e^T.
+ * max_rows bounds the rows of one segment (the token count of the step: a token names an expert at
+ * most once). out in dtype, rows in pair order. */
+int lq_moe_experts(const void* xs, const int32_t* starts, const int32_t* experts, const int32_t* nseg, int P,
+                   int max_rows, int glu, const uint32_t* w0, const void* s0, const void* b0, const uint32_t* w1,
+                   const void* s1, const void* b1, void* out, int E, int N, int K, int bits, int group_size, int dtype,
+                   void* stream);
+
+/* y (T, D) = sum over slots r of weights[t, r] * ys[pos[t*k + r], :] in float32, slots in order, rounded
+ * to dtype (locals/moe.py:339-348). pos == NULL reads row t*k + r. */
+int lq_moe_combine(const void* ys, const float* weights, const int32_t* pos, void* y, int T, int k, int D, int dtype,
+                   void* stream);
+
+/* Read (and with clear != 0 reset) the device status word kernels OR their LQ_DEV_* codes into
+ * (1 = a bounded wait gave up, 2 = an index check failed, 4 = a TMEM allocation failed). Synchronizes
+ * the current device. Returns the word, or 0xffffffff if the read itself failed. */
+unsigned int lq_device_status(int clear);
+
+/* The last CUDA error string seen by the library (static storage). */
+const char* lq_last_cuda_error(void);
+
+/* Human-readable name of an LQ_* code. */
+const char* lq_strerror(int code);
+
+/* ABI version (major * 100 + minor). */
+int lq_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LQ_H_ */

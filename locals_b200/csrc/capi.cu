@@ -1,0 +1,271 @@
+// The C ABI (include/lq.h): argument checks, then dispatch to the kernel families. Never aborts;
+// every failure is an LQ_E_* code.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "../../include/lq.h"
+#include "lq_host.h"
+#include "qmv.h"
+
+namespace lq {
+void note_cuda_error(cudaError_t e);
+const char* last_cuda_error();
+unsigned int read_status(bool clear);
+int quantize_run(const void* w, int w_dt, int N, int K, int bits, int group, uint32_t* wq, void* s, void* b,
+                 int sb_dt, cudaStream_t st);
+int dequantize_run(const uint32_t* wq, const void* s, const void* b, int N, int K, int bits, int group, int dt,
+                   void* out, cudaStream_t st);
+int router_logits_run(const void* x, int x_dt, const void* w, int w_dt, float* logits, int T, int E, int D,
+                      cudaStream_t st);
+int route_topk_run(const float* logits, int T, int E, int k, int mode, uint32_t* inds, float* weights,
+                   cudaStream_t st);
+int group_run(const uint32_t* inds, int P, int E, int32_t* order, int32_t* starts, int32_t* experts, int32_t* nseg,
+              int32_t* pos, cudaStream_t st);
+int gather_rows_run(const void* x, const int32_t* order, int P, int k, int D, void* xs, cudaStream_t st);
+int combine_run(const void* ys, const float* w, const int32_t* pos, void* y, int T, int k, int D, int dt,
+                cudaStream_t st);
+int tc_run(const void* x, const uint32_t* w, const void* s, const void* b, void* y, int M, int N, int K, int bits,
+           int dtype, const int* p, cudaStream_t st);
+bool tc_shape_ok(int M, int N, int K, int bits);
+}  // namespace lq
+
+using namespace lq;
+
+static inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+static inline bool is16(int dt) { return dt == LQ_F16 || dt == LQ_BF16; }
+
+static int finish(int rc) {
+    if (rc == LQ_E_CUDA) note_cuda_error(cudaGetLastError());
+    return rc;
+}
+
+static int check_common(const void* x, const uint32_t* w, const void* s, const void* b, int M, int N, int K, int bits,
+                        int group_size, int dtype) {
+    if (!x || !w || !s || !b) return LQ_E_ARG;
+    if (!is16(dtype)) return LQ_E_UNSUPPORTED;
+    if (bits != 4 && bits != 8) return LQ_E_UNSUPPORTED;
+    if (group_size != 64) return LQ_E_UNSUPPORTED;
+    if (M < 1 || N < 1 || K < 64 || K % 64) return LQ_E_SHAPE;
+    if (!aligned(x, 16) || !aligned(w, 16) || !aligned(s, 4) || !aligned(b, 4)) return LQ_E_ALIGN;
+    return check_device();
+}
+
+static QmvMats one_matrix(const uint32_t* w, const void* s, const void* b, int rows) {
+    QmvMats m = {};
+    m.w[0] = m.w[1] = w;
+    m.s[0] = m.s[1] = s;
+    m.b[0] = m.b[1] = b;
+    m.rows_total[0] = m.rows_total[1] = rows;
+    return m;
+}
+
+static int qmm_common(const void* x, const uint32_t* w, const void* s, const void* b, int nout, void* const* outs,
+                      const int* widths, int M, int N, int K, int bits, int group_size, int dtype, const lq_cfg* cfg,
+                      void* stream) {
+    int rc = check_common(x, w, s, b, M, N, K, bits, group_size, dtype);
+    if (rc) return rc;
+    if (nout < 1 || nout > 3 || !outs) return LQ_E_ARG;
+    QmvArgs a = {};
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    int acc = 0;
+    for (int i = 0; i < nout; ++i) {
+        if (!outs[i] || widths[i] < 1) return LQ_E_ARG;
+        acc += widths[i];
+        a.out[i] = outs[i];
+        a.seg_end[i] = acc;
+        a.ldo[i] = widths[i];
+    }
+    if (acc != N) return LQ_E_SHAPE;
+    a.nseg_out = nout;
+    const int fam = cfg ? cfg->family : LQ_FAM_AUTO;
+    const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (fam == LQ_FAM_TC || (fam == LQ_FAM_AUTO && M > 64 && nout == 1 && tc_shape_ok(M, N, K, bits))) {
+        if (nout != 1) return LQ_E_UNSUPPORTED;
+        if (!tc_shape_ok(M, N, K, bits)) return LQ_E_SHAPE;
+        return finish(tc_run(x, w, s, b, outs[0], M, N, K, bits, dtype, cfg ? cfg->p : nullptr, st));
+    }
+    if (!qmv_shape_ok(K, bits)) return LQ_E_SHAPE;
+    const QmvMats mats = one_matrix(w, s, b, N);
+    return finish(qmv_run(x, M, mats, 1, a, bits, dtype, (cfg && fam == LQ_FAM_QMV) ? cfg->p : nullptr, M, 1, st));
+}
+
+extern "C" {
+
+int lq_version(void) { return 100; }
+
+const char* lq_strerror(int code) {
+    switch (code) {
+        case LQ_OK: return "ok";
+        case LQ_E_ARG: return "bad argument";
+        case LQ_E_SHAPE: return "unsupported shape";
+        case LQ_E_ALIGN: return "misaligned pointer or stride";
+        case LQ_E_UNSUPPORTED: return "unsupported bits/group/dtype";
+        case LQ_E_CUDA: return "CUDA error";
+        case LQ_E_DEVICE: return "not an sm_100 device";
+        default: return "unknown";
+    }
+}
+
+const char* lq_last_cuda_error(void) { return last_cuda_error(); }
+
+unsigned int lq_device_status(int clear) { return read_status(clear != 0); }
+
+int lq_qmm(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int M, int N, int K,
+           int bits, int group_size, int dtype, const lq_cfg* cfg, void* stream) {
+    void* outs[1] = {y};
+    const int widths[1] = {N};
+    return qmm_common(x, w, scales, biases, 1, outs, widths, M, N, K, bits, group_size, dtype, cfg, stream);
+}
+
+int lq_qmm_split(const void* x, const uint32_t* w, const void* scales, const void* biases, int nout, void* const* outs,
+                 const int* widths, int M, int N, int K, int bits, int group_size, int dtype, const lq_cfg* cfg,
+                 void* stream) {
+    if (!widths) return LQ_E_ARG;
+    return qmm_common(x, w, scales, biases, nout, outs, widths, M, N, K, bits, group_size, dtype, cfg, stream);
+}
+
+int lq_qmm_glu(const void* x, const uint32_t* w_gate, const void* s_gate, const void* b_gate, const uint32_t* w_up,
+               const void* s_up, const void* b_up, void* h, int M, int I, int K, int bits, int group_size, int dtype,
+               const lq_cfg* cfg, void* stream) {
+    int rc = check_common(x, w_gate, s_gate, b_gate, M, I, K, bits, group_size, dtype);
+    if (rc) return rc;
+    if (!w_up || !s_up || !b_up || !h) return LQ_E_ARG;
+    if (!aligned(w_up, 16) || !aligned(s_up, 4) || !aligned(b_up, 4)) return LQ_E_ALIGN;
+    if (!qmv_shape_ok(K, bits)) return LQ_E_SHAPE;
+    QmvArgs a = {};
+    a.M = M;
+    a.N = I;
+    a.K = K;
+    a.out[0] = h;
+    a.seg_end[0] = I;
+    a.ldo[0] = I;
+    a.nseg_out = 1;
+    QmvMats m = {};
+    m.w[0] = w_gate;
+    m.s[0] = s_gate;
+    m.b[0] = b_gate;
+    m.w[1] = w_up;
+    m.s[1] = s_up;
+    m.b[1] = b_up;
+    m.rows_total[0] = m.rows_total[1] = I;
+    const int fam = cfg ? cfg->family : LQ_FAM_AUTO;
+    return finish(qmv_run(x, M, m, 2, a, bits, dtype, (cfg && fam == LQ_FAM_QMV) ? cfg->p : nullptr, M, 1,
+                          reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int lq_quantize(const void* w, int w_dtype, int N, int K, int bits, int group_size, uint32_t* wq, void* scales,
+                void* biases, int sb_dtype, void* stream) {
+    if (!w || !wq || !scales || !biases) return LQ_E_ARG;
+    if (bits < 2 || bits > 8 || (32 % bits) != 0) return LQ_E_UNSUPPORTED;
+    if (group_size < 32 / bits || group_size % (32 / bits) || K % group_size || N < 1 || K < 1) return LQ_E_SHAPE;
+    if (w_dtype != LQ_F32 && !is16(w_dtype)) return LQ_E_ARG;
+    if (sb_dtype != LQ_F32 && !is16(sb_dtype)) return LQ_E_ARG;
+    int rc = check_device();
+    if (rc) return rc;
+    return finish(quantize_run(w, w_dtype, N, K, bits, group_size, wq, scales, biases, sb_dtype,
+                               reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int lq_dequantize(const uint32_t* wq, const void* scales, const void* biases, int N, int K, int bits, int group_size,
+                  int dtype, void* w_out, void* stream) {
+    if (!wq || !scales || !biases || !w_out) return LQ_E_ARG;
+    if (bits < 2 || bits > 8 || (32 % bits) != 0) return LQ_E_UNSUPPORTED;
+    if (group_size < 32 / bits || K % group_size || N < 1 || K < 1) return LQ_E_SHAPE;
+    if (dtype != LQ_F32 && !is16(dtype)) return LQ_E_ARG;
+    int rc = check_device();
+    if (rc) return rc;
+    return finish(dequantize_run(wq, scales, biases, N, K, bits, group_size, dtype, w_out,
+                                 reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int lq_router_logits(const void* x, int x_dtype, const void* w, int w_dtype, float* logits, int T, int E, int D,
+                     void* stream) {
+    if (!x || !w || !logits) return LQ_E_ARG;
+    if (!is16(x_dtype) || !is16(w_dtype)) return LQ_E_UNSUPPORTED;
+    if (T < 1 || E < 1 || D < 8 || D % 8) return LQ_E_SHAPE;
+    if (!aligned(x, 16) || !aligned(w, 16)) return LQ_E_ALIGN;
+    int rc = check_device();
+    if (rc) return rc;
+    return finish(router_logits_run(x, x_dtype, w, w_dtype, logits, T, E, D, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int lq_route_topk(const float* logits, int T, int E, int k, int mode, uint32_t* inds, float* weights, void* stream) {
+    if (!logits || !inds || !weights) return LQ_E_ARG;
+    if (mode != 0 && mode != 1) return LQ_E_ARG;
+    if (T < 1 || E < 1 || E > 1024 || k < 1 || k > 32 || k > E) return LQ_E_SHAPE;
+    int rc = check_device();
+    if (rc) return rc;
+    return finish(route_topk_run(logits, T, E, k, mode, inds, weights, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int lq_moe_group(const uint32_t* inds, int P, int E, int32_t* order, int32_t* starts, int32_t* experts, int32_t* nseg,
+                 int32_t* pos, void* stream) {
+    if (!inds || !order || !starts || !experts || !nseg) return LQ_E_ARG;
+    if (P < 1 || E < 1 || E > 8192) return LQ_E_SHAPE;
+    int rc = check_device();
+    if (rc) return rc;
+    return finish(group_run(inds, P, E, order, starts, experts, nseg, pos, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int lq_moe_gather(const void* x, const int32_t* order, int P, int k, int D, void* xs, void* stream) {
+    if (!x || !order || !xs) return LQ_E_ARG;
+    if (P < 1 || k < 1 || D < 8 || D % 8) return LQ_E_SHAPE;
+    if (!aligned(x, 16) || !aligned(xs, 16)) return LQ_E_ALIGN;
+    int rc = check_device();
+    if (rc) return rc;
+    return finish(gather_rows_run(x, order, P, k, D, xs, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int lq_moe_experts(const void* xs, const int32_t* starts, const int32_t* experts, const int32_t* nseg, int P,
+                   int max_rows, int glu, const uint32_t* w0, const void* s0, const void* b0, const uint32_t* w1,
+                   const void* s1, const void* b1, void* out, int E, int N, int K, int bits, int group_size, int dtype,
+                   void* stream) {
+    int rc = check_common(xs, w0, s0, b0, P, N, K, bits, group_size, dtype);
+    if (rc) return rc;
+    if (!starts || !experts || !nseg || !out) return LQ_E_ARG;
+    if (glu && (!w1 || !s1 || !b1)) return LQ_E_ARG;
+    if (glu && (!aligned(w1, 16) || !aligned(s1, 4) || !aligned(b1, 4))) return LQ_E_ALIGN;
+    if (E < 1 || max_rows < 1) return LQ_E_SHAPE;
+    if (!qmv_shape_ok(K, bits)) return LQ_E_SHAPE;
+    if (int64_t(E) * N > INT32_MAX) return LQ_E_SHAPE;
+    QmvArgs a = {};
+    a.M = P;
+    a.N = N;
+    a.K = K;
+    a.out[0] = out;
+    a.seg_end[0] = N;
+    a.ldo[0] = N;
+    a.nseg_out = 1;
+    a.grouped = 1;
+    a.starts = starts;
+    a.experts = experts;
+    a.nseg = nseg;
+    a.n_experts = E;
+    QmvMats m = {};
+    m.w[0] = w0;
+    m.s[0] = s0;
+    m.b[0] = b0;
+    m.w[1] = glu ? w1 : w0;
+    m.s[1] = glu ? s1 : s0;
+    m.b[1] = glu ? b1 : b0;
+    m.rows_total[0] = m.rows_total[1] = E * N;
+    const int nseg_grid = E < P ? E : P;
+    return finish(qmv_run(xs, P, m, glu ? 2 : 1, a, bits, dtype, nullptr, max_rows, nseg_grid,
+                          reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int lq_moe_combine(const void* ys, const float* weights, const int32_t* pos, void* y, int T, int k, int D, int dtype,
+                   void* stream) {
+    if (!ys || !weights || !y) return LQ_E_ARG;
+    if (!is16(dtype)) return LQ_E_UNSUPPORTED;
+    if (T < 1 || k < 1 || D < 1) return LQ_E_SHAPE;
+    int rc = check_device();
+    if (rc) return rc;
+    return finish(combine_run(ys, weights, pos, y, T, k, D, dtype, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

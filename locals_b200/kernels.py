@@ -1,0 +1,230 @@
+"""Quantized-linear dispatch for MLX affine weights on B200 (the counterpart of the reference's
+locals/kernels.py).
+
+The reference routes every 4-bit quantized linear through ``_linear_call_inner``
+(locals/kernels.py:1031-1054): prefill-size inputs (M >= PREFILL_M = 128) to a dequantize + dense
+GEMM or MLX's quantized GEMM (locals/kernels.py:854-866,1020-1025), few-row inputs to the autotuned
+fastest small-M kernel (``_small_matmul`` -> ``_choose`` -> ``_launcher``, locals/kernels.py:516-621,
+797-807), everything else to ``mx.quantized_matmul``. Here the same contract holds --
+``launch(choice, M, K, N, dtype) -> f(x, w, scales, biases) -> y`` with unchanged MLX tensors -- but
+every path is a hand-written sm_100a kernel of liblq.so:
+
+* ``("qmv", MT, R, KS, NS)`` -- decode family (TMA-staged packed weights, register dequant into
+  mma.sync fragments, cluster split-K), any M (weights streamed once per 64 rows);
+* ``("tc", ...)`` -- prefill family (dequantized tiles in shared memory feeding tcgen05.mma with
+  TMEM accumulators), M >= 128.
+
+There is no CPU or library fallback: a shape the kernels reject raises ``LQError``.
+"""
+
+from __future__ import annotations
+
+import threading
+from typing import Callable, Optional, Sequence, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import call
+
+PREFILL_M = 128  # locals/kernels.py:854: from this many rows the prefill family computes the layer
+MAX_SMALL_M = 64  # the decode family's register tiles hold up to 64 rows per pass
+
+_DT = {torch.float16: _lib.F16, torch.bfloat16: _lib.BF16, torch.float32: _lib.F32}
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DT[dt]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dt}") from None
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _check_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if not t.is_cuda:
+            raise ValueError("locals_b200 kernels take CUDA tensors")
+        if not t.is_contiguous():
+            raise ValueError("locals_b200 kernels take contiguous tensors")
+
+
+# ---- format ------------------------------------------------------------------------------------
+
+def quantize(w: torch.Tensor, group_size: int = 64, bits: int = 4, dtype: Optional[torch.dtype] = None):
+    """MLX affine quantization (mx.quantize) of w (N, K) on the GPU: (wq uint32 (N, K*bits/32),
+    scales, biases (N, K/group_size) in ``dtype``, default w's dtype)."""
+    _check_cuda(w)
+    N, K = w.shape
+    dtype = dtype or w.dtype
+    wq = torch.empty((N, K * bits // 32), dtype=torch.int32, device=w.device)
+    s = torch.empty((N, K // group_size), dtype=dtype, device=w.device)
+    b = torch.empty_like(s)
+    call("lq_quantize", w.data_ptr(), dtype_code(w.dtype), N, K, bits, group_size, wq.data_ptr(), s.data_ptr(),
+         b.data_ptr(), dtype_code(dtype), _stream())
+    return wq, s, b  # (uint32 words carried as int32: the same bits)
+
+
+def dequantize(wq: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, group_size: int = 64,
+               bits: int = 4) -> torch.Tensor:
+    """mx.dequantize: (N, K) in the scales' dtype."""
+    _check_cuda(wq, scales, biases)
+    N = wq.shape[0]
+    K = wq.shape[1] * 32 // bits
+    out = torch.empty((N, K), dtype=scales.dtype, device=wq.device)
+    call("lq_dequantize", wq.data_ptr(), scales.data_ptr(), biases.data_ptr(), N, K, bits, group_size,
+         dtype_code(scales.dtype), out.data_ptr(), _stream())
+    return out
+
+
+# ---- matmul ------------------------------------------------------------------------------------
+
+_FAMILY = {"auto": _lib.FAM_AUTO, "qmv": _lib.FAM_QMV, "tc": _lib.FAM_TC}
+
+
+def _cfg(choice: Optional[Sequence]):
+    if choice is None:
+        return None
+    fam = _FAMILY[choice[0]]
+    return _lib.cfg(fam, *choice[1:])
+
+
+def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+                     transpose: bool = True, group_size: int = 64, bits: int = 4,
+                     choice: Optional[Sequence] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y = x . dequant(w)^T (mx.quantized_matmul(x, w, scales, biases, transpose=True, group_size, bits))
+    for x (..., K) fp16/bf16. ``choice`` = ("qmv", MT, R, KS, NS) / ("tc", ...) / None (auto)."""
+    if not transpose:
+        raise NotImplementedError("only transpose=True (the layout of every reference call site)")
+    shape = x.shape
+    K = shape[-1]
+    x2 = x.reshape(-1, K)
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    N = w.shape[0]
+    _check_cuda(x2, w, scales, biases)
+    if scales.dtype != x.dtype or biases.dtype != x.dtype:
+        raise TypeError("scales and biases must have the activations' dtype")
+    y = out if out is not None else torch.empty((M, N), dtype=x.dtype, device=x.device)
+    call("lq_qmm", x2.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(), y.data_ptr(), M, N, K, bits,
+         group_size, dtype_code(x.dtype), _cfg(choice), _stream())
+    return y.reshape(*shape[:-1], N)
+
+
+def qmm_split(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+              widths: Sequence[int], group_size: int = 64, bits: int = 4,
+              choice: Optional[Sequence] = None) -> Tuple[torch.Tensor, ...]:
+    """One fused projection whose output columns go to len(widths) separate (M, width) tensors."""
+    K = x.shape[-1]
+    x2 = x.reshape(-1, K).contiguous()
+    M, N = x2.shape[0], w.shape[0]
+    _check_cuda(x2, w, scales, biases)
+    outs = [torch.empty((M, wd), dtype=x.dtype, device=x.device) for wd in widths]
+    import ctypes
+    ptrs = (ctypes.c_void_p * len(outs))(*[o.data_ptr() for o in outs])
+    wds = (ctypes.c_int * len(outs))(*widths)
+    call("lq_qmm_split", x2.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(), len(outs), ptrs, wds, M,
+         N, K, bits, group_size, dtype_code(x.dtype), _cfg(choice), _stream())
+    return tuple(o.reshape(*x.shape[:-1], o.shape[-1]) for o in outs)
+
+
+def qmm_glu(x: torch.Tensor, gate: Tuple[torch.Tensor, torch.Tensor, torch.Tensor],
+            up: Tuple[torch.Tensor, torch.Tensor, torch.Tensor], group_size: int = 64, bits: int = 4,
+            choice: Optional[Sequence] = None, rows: Optional[int] = None) -> torch.Tensor:
+    """swiglu(x . gate^T, x . up^T) in one kernel (gate/up: (weight, scales, biases), each (I, ...)
+    or views into a concatenated gate||up)."""
+    K = x.shape[-1]
+    x2 = x.reshape(-1, K).contiguous()
+    M = x2.shape[0]
+    I = rows if rows is not None else gate[0].shape[0]
+    _check_cuda(x2)
+    h = torch.empty((M, I), dtype=x.dtype, device=x.device)
+    call("lq_qmm_glu", x2.data_ptr(), gate[0].data_ptr(), gate[1].data_ptr(), gate[2].data_ptr(), up[0].data_ptr(),
+         up[1].data_ptr(), up[2].data_ptr(), h.data_ptr(), M, I, K, bits, group_size, dtype_code(x.dtype),
+         _cfg(choice), _stream())
+    return h.reshape(*x.shape[:-1], I)
+
+
+# ---- the reference's launcher contract -----------------------------------------------------------
+
+_LAUNCH: dict = {}
+
+
+def launch(choice: Sequence, M: int, K: int, N: int, dtype: torch.dtype, bits: int = 4,
+           group_size: int = 64) -> Callable:
+    """A cached closure ``f(x2, w, scales, biases) -> y`` for one tuning choice, as the reference's
+    ``_launcher(choice, M, K, N, dtype)`` (locals/kernels.py:516-576)."""
+    key = (tuple(choice), M, K, N, dtype, bits, group_size)
+    f = _LAUNCH.get(key)
+    if f is None:
+        ch = tuple(choice)
+
+        def f(x2, w, sc, bi, _ch=ch):
+            return quantized_matmul(x2, w, sc, bi, group_size=group_size, bits=bits, choice=_ch)
+
+        _LAUNCH[key] = f
+    return f
+
+
+def candidates(M: int, K: int, N: int, bits: int = 4) -> list:
+    """Tuning candidates for one shape (the analogue of locals/kernels.py:654-674)."""
+    out = []
+    if M <= MAX_SMALL_M:
+        mts = [mt for mt in (1, 2, 4, 8) if 8 * mt >= min(M, 64)][:2]
+        for mt in mts:
+            for r in ((1, 2) if (mt <= 2 and bits == 4) else (1,)):
+                for ks in (1, 2, 4, 8):
+                    if ks <= max(1, K // 512):
+                        out.append(("qmv", mt, r, ks, 0))
+    if M >= PREFILL_M:
+        out.append(("tc",))
+    return out
+
+
+# ---- a quantized linear layer ----------------------------------------------------------------------
+
+class QuantizedLinear:
+    """MLX QuantizedLinear's tensors (weight uint32 (N, K*bits/32), scales, biases (N, K/64)) with the
+    reference's routing (locals/kernels.py:1031-1054): the tuned choice for (N, K, M, dtype) if one is
+    cached (locals_b200.tune), else the kernel library's own pick."""
+
+    def __init__(self, weight: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, bits: int = 4,
+                 group_size: int = 64, bias: Optional[torch.Tensor] = None):
+        self.weight, self.scales, self.biases = weight, scales, biases
+        self.bits, self.group_size, self.bias = bits, group_size, bias
+
+    @property
+    def out_features(self) -> int:
+        return self.weight.shape[0]
+
+    @property
+    def in_features(self) -> int:
+        return self.weight.shape[1] * 32 // self.bits
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        from . import tune
+
+        M = x.numel() // x.shape[-1]
+        choice = tune.lookup(self.out_features, self.in_features, M, x.dtype, self.bits)
+        y = quantized_matmul(x, self.weight, self.scales, self.biases, group_size=self.group_size, bits=self.bits,
+                             choice=choice)
+        if self.bias is not None:
+            y = y + self.bias
+        return y
+
+
+_STATUS_LOCK = threading.Lock()
+
+
+def device_status(clear: bool = True) -> int:
+    """The kernels' device status word (0 = no bounded wait gave up, no index check failed)."""
+    with _STATUS_LOCK:
+        return _lib.device_status(clear)

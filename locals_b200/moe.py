@@ -1,0 +1,134 @@
+"""Routed mixture-of-experts on MLX affine experts (the counterpart of the reference's locals/moe.py
+router/routing and locals/moe_kernel.py grouped experts; config: mlx-lm's SwitchGLU block).
+
+One step: router logits in float32 (locals/moe.py:86-139) -> top-k with softmax (or the reference's
+sigmoid, locals/moe.py:36-82) renormalised -> counting sort of the (token, slot) pairs by expert
+(locals/moe_kernel.py:28-66) -> the pairs' tokens gathered in expert order -> grouped gate/up +
+SwiGLU (each used expert's weights read once for all its pairs, locals/moe_kernel.py:1-12) ->
+grouped down projection -> weighted combine over each token's slots in float32 (locals/moe.py:339-348).
+Every stage is a liblq.so kernel; buffers are allocated here (torch), never by the library.
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Sequence, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import call
+from .kernels import _check_cuda, _stream, dtype_code
+
+SOFTMAX, SIGMOID = 0, 1
+
+
+def router_logits(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """float32 x (..., D) . w (E, D)^T of 16-bit x and w (their dtypes may differ)."""
+    D = x.shape[-1]
+    x2 = x.reshape(-1, D).contiguous()
+    _check_cuda(x2, w)
+    T, E = x2.shape[0], w.shape[0]
+    out = torch.empty((T, E), dtype=torch.float32, device=x.device)
+    call("lq_router_logits", x2.data_ptr(), dtype_code(x.dtype), w.data_ptr(), dtype_code(w.dtype), out.data_ptr(), T,
+         E, D, _stream())
+    return out.reshape(*x.shape[:-1], E)
+
+
+def route_topk(logits: torch.Tensor, k: int, mode: int = SOFTMAX) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(inds int32 (T, k), weights float32 (T, k)) of float32 logits (T, E)."""
+    E = logits.shape[-1]
+    l2 = logits.reshape(-1, E).contiguous()
+    _check_cuda(l2)
+    T = l2.shape[0]
+    inds = torch.empty((T, k), dtype=torch.int32, device=logits.device)
+    wts = torch.empty((T, k), dtype=torch.float32, device=logits.device)
+    call("lq_route_topk", l2.data_ptr(), T, E, k, mode, inds.data_ptr(), wts.data_ptr(), _stream())
+    return inds, wts
+
+
+def group(inds: torch.Tensor, E: int):
+    """(order, starts, experts, nseg, pos) of the flat expert ids (the reference's group(),
+    locals/moe_kernel.py:191-197, plus the inverse permutation)."""
+    flat = inds.reshape(-1).contiguous()
+    _check_cuda(flat)
+    P = flat.numel()
+    S = min(E, P)
+    dev = inds.device
+    order = torch.empty(P, dtype=torch.int32, device=dev)
+    pos = torch.empty(P, dtype=torch.int32, device=dev)
+    starts = torch.empty(S + 1, dtype=torch.int32, device=dev)
+    experts = torch.empty(S, dtype=torch.int32, device=dev)
+    nseg = torch.empty(1, dtype=torch.int32, device=dev)
+    call("lq_moe_group", flat.data_ptr(), P, E, order.data_ptr(), starts.data_ptr(), experts.data_ptr(),
+         nseg.data_ptr(), pos.data_ptr(), _stream())
+    return order, starts, experts, nseg, pos
+
+
+def gather(x: torch.Tensor, order: torch.Tensor, k: int) -> torch.Tensor:
+    D = x.shape[-1]
+    P = order.numel()
+    xs = torch.empty((P, D), dtype=x.dtype, device=x.device)
+    call("lq_moe_gather", x.data_ptr(), order.data_ptr(), P, k, D, xs.data_ptr(), _stream())
+    return xs
+
+
+def experts(xs: torch.Tensor, grouping, mats: Sequence, N: int, max_rows: int, bits: int = 4,
+            group_size: int = 64) -> torch.Tensor:
+    """Grouped projections over pair-ordered rows xs (P, K): mats = [gate, up] (SwiGLU) or [w];
+    each (weight (E, N, K*bits/32), scales (E, N, K/64), biases)."""
+    order, starts, experts_, nseg, _ = grouping
+    P, K = xs.shape
+    E = mats[0][0].shape[0]
+    glu = len(mats) == 2
+    w0, s0, b0 = mats[0]
+    w1, s1, b1 = mats[1] if glu else (w0, s0, b0)
+    out = torch.empty((P, N), dtype=xs.dtype, device=xs.device)
+    call("lq_moe_experts", xs.data_ptr(), starts.data_ptr(), experts_.data_ptr(), nseg.data_ptr(), P, max_rows,
+         1 if glu else 0, w0.data_ptr(), s0.data_ptr(), b0.data_ptr(), w1.data_ptr(), s1.data_ptr(), b1.data_ptr(),
+         out.data_ptr(), E, N, K, bits, group_size, dtype_code(xs.dtype), _stream())
+    return out
+
+
+def combine(ys: torch.Tensor, weights: torch.Tensor, pos: Optional[torch.Tensor]) -> torch.Tensor:
+    T, k = weights.shape
+    D = ys.shape[-1]
+    y = torch.empty((T, D), dtype=ys.dtype, device=ys.device)
+    call("lq_moe_combine", ys.data_ptr(), weights.data_ptr(), None if pos is None else pos.data_ptr(), y.data_ptr(),
+         T, k, D, dtype_code(ys.dtype), _stream())
+    return y
+
+
+def switch_glu(x: torch.Tensor, inds: torch.Tensor, gate, up, down, bits: int = 4, group_size: int = 64,
+               grouping=None) -> torch.Tensor:
+    """mlx-lm SwitchGLU for rows x (M, D) and experts inds (M, k): (M*k, D) rows in pair order, with the
+    grouping used (the reference's switch_glu, locals/moe_kernel.py:230-239)."""
+    M, k = inds.shape
+    E = gate[0].shape[0]
+    I = gate[0].shape[1]
+    D = x.shape[-1]
+    if grouping is None:
+        grouping = group(inds, E)
+    xs = gather(x, grouping[0], k)
+    h = experts(xs, grouping, [gate, up], I, max_rows=M, bits=bits, group_size=group_size)
+    return experts(h, grouping, [down], D, max_rows=M, bits=bits, group_size=group_size)
+
+
+class MoELayer:
+    """Router + top-k experts + combine over stacked MLX-affine experts."""
+
+    def __init__(self, router_w: torch.Tensor, gate, up, down, top_k: int, mode: int = SOFTMAX, bits: int = 4,
+                 group_size: int = 64):
+        self.router_w, self.gate, self.up, self.down = router_w, gate, up, down
+        self.top_k, self.mode, self.bits, self.group_size = top_k, mode, bits, group_size
+        self.n_experts = gate[0].shape[0]
+
+    def route(self, x: torch.Tensor):
+        return route_topk(router_logits(x, self.router_w), self.top_k, self.mode)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        D = x.shape[-1]
+        x2 = x.reshape(-1, D).contiguous()
+        inds, wts = self.route(x2)
+        grouping = group(inds, self.n_experts)
+        ys = switch_glu(x2, inds, self.gate, self.up, self.down, self.bits, self.group_size, grouping)
+        return combine(ys, wts, grouping[4]).reshape(x.shape)
