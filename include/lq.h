@@ -34,7 +34,7 @@ extern "C" {
 
 /* Kernel families, the analogue of the reference's tuning choices (locals/kernels.py:136-144). */
 #define LQ_FAM_AUTO 0   /* pick by shape (M <= 64: QMV, else TC) */
-#define LQ_FAM_QMV 1    /* decode: TMA-staged packed weights, register dequant, mma.sync; p = {MT, R, KS, NS} */
+#define LQ_FAM_QMV 1    /* decode: TMA-staged packed weights, register dequant, mma.sync; p = {MT, WK, KS, NS} */
 #define LQ_FAM_TC 2     /* prefill: dequant tiles into shared memory, tcgen05.mma into TMEM */
 
 typedef struct lq_cfg {

@@ -76,6 +76,7 @@ const DeviceInfo& device_info() {
             di.major = p.major;
             di.minor = p.minor;
             di.smem_optin = p.sharedMemPerBlockOptin;
+            di.smem_per_sm = p.sharedMemPerMultiprocessor;
             di.device = dev;
         }
     }

@@ -21,6 +21,7 @@ struct DeviceInfo {
     int sm_count = 0;
     int major = 0, minor = 0;
     size_t smem_optin = 0;
+    size_t smem_per_sm = 0;
 };
 
 // Properties of the current device (cached per device).

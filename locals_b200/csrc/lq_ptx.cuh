@@ -159,6 +159,11 @@ __device__ __forceinline__ float ld_dsmem_f(uint32_t addr) {
     return v;
 }
 
+// Barrier among `nthreads` threads (a multiple of 32) on hardware barrier `id` (1..15; 0 is __syncthreads).
+__device__ __forceinline__ void named_barrier(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // ---- bit tricks -----------------------------------------------------------------------------
 
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t magic) {

@@ -39,25 +39,33 @@
 
 namespace lq {
 
-constexpr int QMV_BK = 512;       // K values per stage (8 groups of 64)
-constexpr int QMV_CONSUMERS = 4;  // consumer warps
-constexpr int QMV_THREADS = 32 * (QMV_CONSUMERS + 1);
+constexpr int QMV_CW = 8;  // consumer warps
+constexpr int QMV_THREADS = 32 * (QMV_CW + 1);
 constexpr int QMV_MAX_STAGES = 8;
 
-template <typename T, int BITS, int MT, int R, int NMAT>
+// Tile geometry. A stage holds 256 bytes of packed words per weight row (512 K values at 4 bits, 256 at
+// 8 bits): two 128-byte swizzle segments. Each consumer warp owns one 16-row MMA fragment; WK warps
+// share a fragment and split each stage's four 64-byte iterations between them (K split inside the CTA,
+// summed through shared memory at the end), so a CTA has 8 / WK fragments = BN rows.
+template <typename T, int BITS, int MT, int WK, int NMAT>
 struct QmvShape {
-    static constexpr int BN = 64 * R;                  // rows of each matrix per CTA
-    static constexpr int MTOK = 8 * MT;                // token slots per pass
-    static constexpr int WPR = QMV_BK * BITS / 32;     // packed words per row per stage
-    static constexpr int SEGW = WPR / 32;              // 128-byte segments per row per stage
-    static constexpr int W_BYTES = BN * WPR * 4;       // one matrix
-    static constexpr int SB_BYTES = BN * 16;           // 8 groups of 16-bit scales (or biases)
-    static constexpr int X_BYTES = MTOK * QMV_BK * 2;  // x slice: 8 swizzled 64-value segments
+    static constexpr int RF = QMV_CW / WK;              // row fragments per CTA
+    static constexpr int BN = 16 * RF;                  // rows of each matrix per CTA
+    static constexpr int MTOK = 8 * MT;                 // token slots per pass
+    static constexpr int BK = 2048 / BITS;              // K values per stage
+    static constexpr int GPS = BK / 64;                 // groups per stage
+    static constexpr int SBROW = GPS * 2;               // bytes per row of a scale (or bias) tile
+    static constexpr int W_BYTES = BN * 256;            // one matrix
+    static constexpr int SB_BYTES = BN * SBROW;         // one array of one matrix
+    static constexpr int X_BYTES = MTOK * BK * 2;       // x slice: BK / 64 swizzled 64-value segments
     static constexpr int TMA_BYTES = NMAT * W_BYTES + X_BYTES;
-    static constexpr int STAGE_BYTES = NMAT * (W_BYTES + 2 * SB_BYTES) + X_BYTES;
-    static constexpr int IT = (BITS == 4) ? 4 : 8;     // inner iterations per stage (16 words a row each)
+    static constexpr int RAW_STAGE = NMAT * (W_BYTES + 2 * SB_BYTES) + X_BYTES;
+    static constexpr int STAGE_BYTES = (RAW_STAGE + 1023) / 1024 * 1024;
+    static constexpr int IT = 4;                        // 64-byte iterations per stage
+    static constexpr int ITW = IT / WK;                 // iterations per warp per stage
+    static constexpr int RED_BYTES = (WK - 1) * NMAT * BN * MTOK * 4;
     static constexpr int PART_BYTES = NMAT * BN * MTOK * 4;
-    static_assert(W_BYTES % 1024 == 0 && X_BYTES % 1024 == 0 && SB_BYTES % 1024 == 0, "1 KB alignment");
+    static_assert(W_BYTES % 1024 == 0 && X_BYTES % 1024 == 0, "1 KB alignment of swizzled tiles");
 };
 
 // Fragment row g of a 16-row MMA tile -> tile row. Rows 2i and 2i+1 of a quarter-warp differ in bit 2
@@ -98,12 +106,130 @@ __device__ __forceinline__ void store_out(const QmvArgs& a, int row, int n, floa
         reinterpret_cast<__half*>(a.out[seg])[off] = __float2half_rn(v);
 }
 
-template <typename T, int BITS, int MT, int R, int NMAT>
-__global__ void __launch_bounds__(QMV_THREADS, 1)
+// One 64-byte iteration of one warp: 16 rows x (128 K at 4 bits | 64 K at 8 bits) against MT token tiles.
+template <typename T, int BITS, int MT, int WK, int NMAT>
+__device__ __forceinline__ void qmv_iteration(float (&acc)[NMAT][MT][4], uint32_t st, int it, int ra, int g, int t) {
+    using S = QmvShape<T, BITS, MT, WK, NMAT>;
+    using TR = F16Traits<T>;
+    constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+    const int rb = ra + 8;
+    const uint32_t xs = st + NMAT * S::W_BYTES;
+    const uint32_t sbs = xs + S::X_BYTES;
+    const int wseg = it >> 1;
+    const int wchunk = 4 * (it & 1) + t;
+    const int grp = (BITS == 4) ? (2 * it + (t >> 1)) : it;
+    uint4 wa[NMAT], wb[NMAT];
+    uint32_t s2a[NMAT], b2a[NMAT], s2b[NMAT], b2b[NMAT];
+    float sfa[NMAT], bfa[NMAT], sfb[NMAT], bfb[NMAT];
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m) {
+        const uint32_t wbase = st + m * S::W_BYTES + wseg * (S::BN * 128);
+        wa[m] = lds128(wbase + ra * 128 + ((wchunk ^ (ra & 7)) << 4));
+        wb[m] = lds128(wbase + rb * 128 + ((wchunk ^ (rb & 7)) << 4));
+        const uint32_t sp = sbs + 2 * m * S::SB_BYTES;
+        const uint32_t bp = sp + S::SB_BYTES;
+        const uint32_t sa = lds_u16(sp + ra * S::SBROW + grp * 2), ba = lds_u16(bp + ra * S::SBROW + grp * 2);
+        const uint32_t sb = lds_u16(sp + rb * S::SBROW + grp * 2), bb = lds_u16(bp + rb * S::SBROW + grp * 2);
+        if constexpr (BITS == 8 && kBF16) {
+            sfa[m] = TR::to_f32(sa);
+            bfa[m] = TR::to_f32(ba);
+            sfb[m] = TR::to_f32(sb);
+            bfb[m] = TR::to_f32(bb);
+        } else {
+            s2a[m] = prmt(sa, sa, 0x1010);
+            b2a[m] = prmt(ba, ba, 0x1010);
+            s2b[m] = prmt(sb, sb, 0x1010);
+            b2b[m] = prmt(bb, bb, 0x1010);
+        }
+    }
+    if constexpr (BITS == 4) {
+        const int xseg = 2 * it + (t >> 1);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint32_t xp[MT][4];
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                const int tok = 8 * mt + g;
+                const int xc = 4 * (t & 1) + j;
+                const uint4 u = lds128(xs + xseg * (S::MTOK * 128) + tok * 128 + ((xc ^ (tok & 7)) << 4));
+                xp[mt][0] = prmt(u.x, u.z, 0x5410);  // (x0, x4)
+                xp[mt][1] = prmt(u.x, u.z, 0x7632);  // (x1, x5)
+                xp[mt][2] = prmt(u.y, u.w, 0x5410);  // (x2, x6)
+                xp[mt][3] = prmt(u.y, u.w, 0x7632);  // (x3, x7)
+            }
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) {
+                const uint32_t wva = (j == 0) ? wa[m].x : (j == 1) ? wa[m].y : (j == 2) ? wa[m].z : wa[m].w;
+                const uint32_t wvb = (j == 0) ? wb[m].x : (j == 1) ? wb[m].y : (j == 2) ? wb[m].z : wb[m].w;
+                uint32_t pa[4], pb[4];
+#pragma unroll
+                for (int p = 0; p < 4; ++p) {  // codes (p, p + 4) of the word
+                    pa[p] = TR::sub_magic_fma(lop3_and_or(wva >> (4 * p), 0x000F000Fu, TR::kMagic2), s2a[m], b2a[m]);
+                    pb[p] = TR::sub_magic_fma(lop3_and_or(wvb >> (4 * p), 0x000F000Fu, TR::kMagic2), s2b[m], b2b[m]);
+                }
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    mma_16816<T>(acc[m][mt], pa[0], pb[0], pa[1], pb[1], xp[mt][0], xp[mt][1]);
+                    mma_16816<T>(acc[m][mt], pa[2], pb[2], pa[3], pb[3], xp[mt][2], xp[mt][3]);
+                }
+            }
+        }
+    } else {
+        const int xseg = it;
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+            uint4 xu[MT];
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                const int tok = 8 * mt + g;
+                const int xc = 2 * t + jj;
+                xu[mt] = lds128(xs + xseg * (S::MTOK * 128) + tok * 128 + ((xc ^ (tok & 7)) << 4));
+            }
+#pragma unroll
+            for (int jh = 0; jh < 2; ++jh) {
+                const int j = 2 * jj + jh;
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m) {
+                    const uint32_t wva = (j == 0) ? wa[m].x : (j == 1) ? wa[m].y : (j == 2) ? wa[m].z : wa[m].w;
+                    const uint32_t wvb = (j == 0) ? wb[m].x : (j == 1) ? wb[m].y : (j == 2) ? wb[m].z : wb[m].w;
+                    uint32_t lo_a, hi_a, lo_b, hi_b;
+                    if constexpr (kBF16) {
+                        // a byte code as float: OR it into the mantissa of 2^23, subtract 2^23
+                        float fa[4], fb[4];
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            fa[q] = fmaf(__uint_as_float(prmt(wva, 0x4B000000u, 0x7540u + q)) - 8388608.0f, sfa[m],
+                                         bfa[m]);
+                            fb[q] = fmaf(__uint_as_float(prmt(wvb, 0x4B000000u, 0x7540u + q)) - 8388608.0f, sfb[m],
+                                         bfb[m]);
+                        }
+                        lo_a = cvt_bf16x2(fa[1], fa[0]);
+                        hi_a = cvt_bf16x2(fa[3], fa[2]);
+                        lo_b = cvt_bf16x2(fb[1], fb[0]);
+                        hi_b = cvt_bf16x2(fb[3], fb[2]);
+                    } else {
+                        lo_a = TR::sub_magic_fma(prmt(wva, 0x64646464u, 0x5140u), s2a[m], b2a[m]);
+                        hi_a = TR::sub_magic_fma(prmt(wva, 0x64646464u, 0x5342u), s2a[m], b2a[m]);
+                        lo_b = TR::sub_magic_fma(prmt(wvb, 0x64646464u, 0x5140u), s2b[m], b2b[m]);
+                        hi_b = TR::sub_magic_fma(prmt(wvb, 0x64646464u, 0x5342u), s2b[m], b2b[m]);
+                    }
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) {
+                        const uint32_t xlo = jh ? xu[mt].z : xu[mt].x;
+                        const uint32_t xhi = jh ? xu[mt].w : xu[mt].y;
+                        mma_16816<T>(acc[m][mt], lo_a, lo_b, hi_a, hi_b, xlo, xhi);
+                    }
+                }
+            }
+        }
+    }
+}
+
+template <typename T, int BITS, int MT, int WK, int NMAT>
+__global__ void __launch_bounds__(QMV_THREADS, (MT * NMAT <= 2) ? 2 : 1)
     qmv_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
                const __grid_constant__ CUtensorMap tm_x, const QmvArgs a) {
-    using S = QmvShape<T, BITS, MT, R, NMAT>;
-    using TR = F16Traits<T>;
+    using S = QmvShape<T, BITS, MT, WK, NMAT>;
     constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -111,7 +237,8 @@ __global__ void __launch_bounds__(QMV_THREADS, 1)
     const int ns = a.ns;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + ns * S::STAGE_BYTES);
     uint64_t* empty = full + QMV_MAX_STAGES;
-    float* part = reinterpret_cast<float*>(smem + ns * S::STAGE_BYTES + 2 * QMV_MAX_STAGES * 8 + 128);
+    float* red = reinterpret_cast<float*>(smem + ns * S::STAGE_BYTES + 2 * QMV_MAX_STAGES * 8);
+    float* part = red + S::RED_BYTES / 4;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * S::BN;
@@ -125,7 +252,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 1)
     if (a.grouped) {
         grid_dep_wait();  // starts / experts / nseg come from the grouping kernel
         const int sgi = blockIdx.z;
-        if (sgi >= a.nseg[0]) return;  // whole cluster shares blockIdx.z: it exits together
+        if (sgi >= a.nseg[0]) return;  // the whole cluster shares blockIdx.z: it exits together
         seg_row0 = a.starts[sgi];
         seg_rows = a.starts[sgi + 1] - seg_row0;
         const int e = a.experts[sgi];
@@ -142,17 +269,25 @@ __global__ void __launch_bounds__(QMV_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < ns; ++s) {
             mbar_init(&full[s], 1 + 32);  // lane 0's expect_tx arrive + 32 cp.async arrivals
-            mbar_init(&empty[s], QMV_CONSUMERS);
+            mbar_init(&empty[s], QMV_CW);
         }
         fence_barrier_init();
     }
     __syncthreads();
 
-    float acc[NMAT][R][MT][4];
+    float acc[NMAT][MT][4];
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+        for (int q = 0; q < MT; ++q)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[m][q][e] = 0.0f;
     bool ok = true;
     const int g = lane >> 2, t = lane & 3;
+    const int rf = warp % S::RF, kq = warp / S::RF;
+    const int ra = 16 * rf + pi_row(g);
 
-    if (warp == QMV_CONSUMERS) {
+    if (warp == QMV_CW) {
         // ------------------------------ producer warp ------------------------------
         const uint64_t pol_w = policy_evict_first();
         const uint64_t pol_x = policy_evict_last();
@@ -163,8 +298,8 @@ __global__ void __launch_bounds__(QMV_THREADS, 1)
         const CUtensorMap* tw[2] = {&tm_w0, &tm_w1};
         const uint32_t smem_base = smem_u32(smem);
         const int kg = a.K / 64;  // groups per row
-        const int vb = a.sb_vec;  // bytes per cp.async (4, 8 or 16)
-        const int units_row = 16 / vb;
+        const int vb = a.sb_vec;  // bytes per cp.async
+        const int units_row = S::SBROW / vb;
         auto load_weights = [&](int i, int s) {
             const uint32_t st = smem_base + s * S::STAGE_BYTES;
             const int c = c_begin + (i % nloc);
@@ -173,21 +308,21 @@ __global__ void __launch_bounds__(QMV_THREADS, 1)
 #pragma unroll
                 for (int m = 0; m < NMAT; ++m)
                     tma_load_3d(smem + s * S::STAGE_BYTES + m * S::W_BYTES, tw[m], &full[s], 0,
-                                wrow0 + n0 + a.row_off[m], c * S::SEGW, pol_w);
+                                wrow0 + n0 + a.row_off[m], c * 2, pol_w);
             }
-            // scales and biases: per matrix 2 arrays x BN rows x 16 bytes
+            // scales and biases: per matrix 2 arrays x BN rows x SBROW bytes
             const int per_mat = 2 * S::BN * units_row;
             for (int u = lane; u < NMAT * per_mat; u += 32) {
                 const int m = u / per_mat, rem = u % per_mat;
                 const int arr = rem / (S::BN * units_row);
                 const int r = (rem / units_row) % S::BN, part_i = rem % units_row;
                 const int grow = wrow0 + n0 + a.row_off[m] + r;
-                const int gcol = c * 8 + part_i * (vb / 2);  // first group of this unit
+                const int gcol = c * S::GPS + part_i * (vb / 2);  // first group of this unit
                 const bool valid = grow < a.rows_total[m] && gcol < kg;
                 const uint8_t* base = reinterpret_cast<const uint8_t*>(arr ? a.bptr[m] : a.sptr[m]);
                 const uint8_t* src = valid ? base + (size_t(grow) * kg + gcol) * 2 : base;
-                const uint32_t dst = st + NMAT * S::W_BYTES + S::X_BYTES + (2 * m + arr) * S::SB_BYTES + r * 16 +
-                                     part_i * vb;
+                const uint32_t dst = st + NMAT * S::W_BYTES + S::X_BYTES + (2 * m + arr) * S::SB_BYTES +
+                                     r * S::SBROW + part_i * vb;
                 cp_async(dst, src, vb, valid);
             }
             cp_async_arrive(&full[s]);
@@ -196,7 +331,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 1)
             if (lane == 0) {
                 const int tb = i / nloc, c = c_begin + (i % nloc);
                 tma_load_3d(smem + s * S::STAGE_BYTES + NMAT * S::W_BYTES, &tm_x, &full[s], 0,
-                            seg_row0 + tb * S::MTOK, c * 8, pol_x);
+                            seg_row0 + tb * S::MTOK, c * (S::BK / 64), pol_x);
             }
         };
         const int pre = total < ns ? total : ns;
@@ -204,185 +339,64 @@ __global__ void __launch_bounds__(QMV_THREADS, 1)
         if (!a.grouped) grid_dep_wait();  // x may be the previous kernel's output
         for (int i = 0; i < pre; ++i) load_x(i, i);
         if (lane == 0) grid_dep_launch();
-        for (int i = pre; i < total; ++i) {
+        for (int i = pre; i < total && ok; ++i) {
             const int s = i % ns;
-            if (!mbar_wait(&empty[s], ((i / ns) - 1) & 1)) {
-                ok = false;
-                break;
-            }
+            ok = mbar_wait(&empty[s], ((i / ns) - 1) & 1);
+            if (!ok) break;
             load_weights(i, s);
             load_x(i, s);
         }
         __syncwarp();
     } else {
         // ------------------------------ consumer warps ------------------------------
-        const int rowa = pi_row(g);  // + 8 for the second half of the fragment
         const uint32_t smem_base = smem_u32(smem);
-        for (int i = 0; i < total && ok; ++i) {
-            if (i % nloc == 0) {
-#pragma unroll
-                for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-                    for (int r = 0; r < R; ++r)
-#pragma unroll
-                        for (int q = 0; q < MT; ++q)
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) acc[m][r][q][e] = 0.0f;
-            }
+        if (!a.grouped) grid_dep_wait();  // (before any output store of this kernel)
+        for (int i = 0; i < total; ++i) {
             const int s = i % ns;
-            if (!mbar_wait(&full[s], (i / ns) & 1)) {
-                ok = false;
-                break;
-            }
-            const uint32_t st = smem_base + s * S::STAGE_BYTES;
-            const uint32_t xs = st + NMAT * S::W_BYTES;
-            const uint32_t sbs = xs + S::X_BYTES;
-#pragma unroll 1
-            for (int it = 0; it < S::IT; ++it) {
-                const int wseg = it >> 1;
-                const int wchunk = 4 * (it & 1) + t;
-                const int grp = (BITS == 4) ? (2 * it + (t >> 1)) : it;
-                uint4 wa[NMAT][R], wb[NMAT][R];
-                uint32_t s2a[NMAT][R], b2a[NMAT][R], s2b[NMAT][R], b2b[NMAT][R];
-                float sfa[NMAT][R], bfa[NMAT][R], sfb[NMAT][R], bfb[NMAT][R];
+            if (ok) ok = mbar_wait(&full[s], (i / ns) & 1);
+            if (ok) {
+                const uint32_t st = smem_base + s * S::STAGE_BYTES;
 #pragma unroll
-                for (int m = 0; m < NMAT; ++m) {
-#pragma unroll
-                    for (int r = 0; r < R; ++r) {
-                        const int ra = warp * 16 * R + 16 * r + rowa, rb = ra + 8;
-                        const uint32_t wbase = st + m * S::W_BYTES + wseg * (S::BN * 128);
-                        wa[m][r] = lds128(wbase + ra * 128 + ((wchunk ^ (ra & 7)) << 4));
-                        wb[m][r] = lds128(wbase + rb * 128 + ((wchunk ^ (rb & 7)) << 4));
-                        const uint32_t sp = sbs + 2 * m * S::SB_BYTES;
-                        const uint32_t bp = sp + S::SB_BYTES;
-                        const uint32_t sa = lds_u16(sp + ra * 16 + grp * 2), ba = lds_u16(bp + ra * 16 + grp * 2);
-                        const uint32_t sb = lds_u16(sp + rb * 16 + grp * 2), bb = lds_u16(bp + rb * 16 + grp * 2);
-                        if constexpr (BITS == 8 && kBF16) {
-                            sfa[m][r] = TR::to_f32(sa);
-                            bfa[m][r] = TR::to_f32(ba);
-                            sfb[m][r] = TR::to_f32(sb);
-                            bfb[m][r] = TR::to_f32(bb);
-                        } else {
-                            s2a[m][r] = prmt(sa, sa, 0x1010);
-                            b2a[m][r] = prmt(ba, ba, 0x1010);
-                            s2b[m][r] = prmt(sb, sb, 0x1010);
-                            b2b[m][r] = prmt(bb, bb, 0x1010);
-                        }
-                    }
-                }
-                if constexpr (BITS == 4) {
-                    const int xseg = 2 * it + (t >> 1);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        uint32_t xp[MT][4];
-#pragma unroll
-                        for (int mt = 0; mt < MT; ++mt) {
-                            const int tok = 8 * mt + g;
-                            const int xc = 4 * (t & 1) + j;
-                            const uint4 u =
-                                lds128(xs + xseg * (S::MTOK * 128) + tok * 128 + ((xc ^ (tok & 7)) << 4));
-                            xp[mt][0] = prmt(u.x, u.z, 0x5410);  // (x0, x4)
-                            xp[mt][1] = prmt(u.x, u.z, 0x7632);  // (x1, x5)
-                            xp[mt][2] = prmt(u.y, u.w, 0x5410);  // (x2, x6)
-                            xp[mt][3] = prmt(u.y, u.w, 0x7632);  // (x3, x7)
-                        }
-#pragma unroll
-                        for (int m = 0; m < NMAT; ++m) {
-#pragma unroll
-                            for (int r = 0; r < R; ++r) {
-                                const uint32_t wva =
-                                    (j == 0) ? wa[m][r].x : (j == 1) ? wa[m][r].y : (j == 2) ? wa[m][r].z : wa[m][r].w;
-                                const uint32_t wvb =
-                                    (j == 0) ? wb[m][r].x : (j == 1) ? wb[m][r].y : (j == 2) ? wb[m][r].z : wb[m][r].w;
-                                uint32_t pa[4], pb[4];
-#pragma unroll
-                                for (int p = 0; p < 4; ++p) {  // codes (p, p + 4) of the word
-                                    pa[p] = TR::sub_magic_fma(lop3_and_or(wva >> (4 * p), 0x000F000Fu, TR::kMagic2),
-                                                              s2a[m][r], b2a[m][r]);
-                                    pb[p] = TR::sub_magic_fma(lop3_and_or(wvb >> (4 * p), 0x000F000Fu, TR::kMagic2),
-                                                              s2b[m][r], b2b[m][r]);
-                                }
-#pragma unroll
-                                for (int mt = 0; mt < MT; ++mt) {
-                                    mma_16816<T>(acc[m][r][mt], pa[0], pb[0], pa[1], pb[1], xp[mt][0], xp[mt][1]);
-                                    mma_16816<T>(acc[m][r][mt], pa[2], pb[2], pa[3], pb[3], xp[mt][2], xp[mt][3]);
-                                }
-                            }
-                        }
-                    }
-                } else {
-                    const int xseg = it;
-#pragma unroll
-                    for (int jj = 0; jj < 2; ++jj) {
-                        uint4 xu[MT];
-#pragma unroll
-                        for (int mt = 0; mt < MT; ++mt) {
-                            const int tok = 8 * mt + g;
-                            const int xc = 2 * t + jj;
-                            xu[mt] = lds128(xs + xseg * (S::MTOK * 128) + tok * 128 + ((xc ^ (tok & 7)) << 4));
-                        }
-#pragma unroll
-                        for (int jh = 0; jh < 2; ++jh) {
-                            const int j = 2 * jj + jh;
-#pragma unroll
-                            for (int m = 0; m < NMAT; ++m) {
-#pragma unroll
-                                for (int r = 0; r < R; ++r) {
-                                    const uint32_t wva = (j == 0)   ? wa[m][r].x
-                                                         : (j == 1) ? wa[m][r].y
-                                                         : (j == 2) ? wa[m][r].z
-                                                                    : wa[m][r].w;
-                                    const uint32_t wvb = (j == 0)   ? wb[m][r].x
-                                                         : (j == 1) ? wb[m][r].y
-                                                         : (j == 2) ? wb[m][r].z
-                                                                    : wb[m][r].w;
-                                    uint32_t lo_a, hi_a, lo_b, hi_b;
-                                    if constexpr (kBF16) {
-                                        // a byte code as float: OR it into the mantissa of 2^23, subtract 2^23
-                                        float fa[4], fb[4];
-#pragma unroll
-                                        for (int q = 0; q < 4; ++q) {
-                                            fa[q] = fmaf(__uint_as_float(prmt(wva, 0x4B000000u, 0x7540u + q)) -
-                                                             8388608.0f,
-                                                         sfa[m][r], bfa[m][r]);
-                                            fb[q] = fmaf(__uint_as_float(prmt(wvb, 0x4B000000u, 0x7540u + q)) -
-                                                             8388608.0f,
-                                                         sfb[m][r], bfb[m][r]);
-                                        }
-                                        lo_a = cvt_bf16x2(fa[1], fa[0]);
-                                        hi_a = cvt_bf16x2(fa[3], fa[2]);
-                                        lo_b = cvt_bf16x2(fb[1], fb[0]);
-                                        hi_b = cvt_bf16x2(fb[3], fb[2]);
-                                    } else {
-                                        lo_a = TR::sub_magic_fma(prmt(wva, 0x64646464u, 0x5140u), s2a[m][r], b2a[m][r]);
-                                        hi_a = TR::sub_magic_fma(prmt(wva, 0x64646464u, 0x5342u), s2a[m][r], b2a[m][r]);
-                                        lo_b = TR::sub_magic_fma(prmt(wvb, 0x64646464u, 0x5140u), s2b[m][r], b2b[m][r]);
-                                        hi_b = TR::sub_magic_fma(prmt(wvb, 0x64646464u, 0x5342u), s2b[m][r], b2b[m][r]);
-                                    }
-#pragma unroll
-                                    for (int mt = 0; mt < MT; ++mt) {
-                                        const uint32_t xlo = jh ? xu[mt].z : xu[mt].x;
-                                        const uint32_t xhi = jh ? xu[mt].w : xu[mt].y;
-                                        mma_16816<T>(acc[m][r][mt], lo_a, lo_b, hi_a, hi_b, xlo, xhi);
-                                    }
-                                }
-                            }
-                        }
-                    }
-                }
+                for (int q = 0; q < S::ITW; ++q) qmv_iteration<T, BITS, MT, WK, NMAT>(acc, st, kq + WK * q, ra, g, t);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
 
-            if (a.ks == 1 && (i % nloc) == nloc - 1) {
-                // token block done: store it (no cluster reduction)
-                const int tb = i / nloc;
-                if (!a.grouped) grid_dep_wait();
+            if ((i % nloc) == nloc - 1) {
+                // token block done: sum the K-split warps of each fragment
+                if constexpr (WK > 1) {
+                    if (kq > 0) {
 #pragma unroll
-                for (int r = 0; r < R; ++r) {
+                        for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    const int row = ra + 8 * (e >> 1), tok = 8 * mt + 2 * t + (e & 1);
+                                    red[(((kq - 1) * NMAT + m) * S::MTOK + tok) * S::BN + row] = acc[m][mt][e];
+                                }
+                    }
+                    named_barrier(1, 32 * QMV_CW);
+                    if (kq == 0) {
+#pragma unroll
+                        for (int q = 1; q < WK; ++q)
+#pragma unroll
+                            for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                                    for (int e = 0; e < 4; ++e) {
+                                        const int row = ra + 8 * (e >> 1), tok = 8 * mt + 2 * t + (e & 1);
+                                        acc[m][mt][e] += red[(((q - 1) * NMAT + m) * S::MTOK + tok) * S::BN + row];
+                                    }
+                    }
+                    named_barrier(1, 32 * QMV_CW);
+                }
+                if (a.ks == 1 && kq == 0 && ok) {
+                    const int tb = i / nloc;
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        const int n = n0 + warp * 16 * R + 16 * r + rowa + 8 * h;
+                        const int n = n0 + ra + 8 * h;
                         if (n >= a.N) continue;
 #pragma unroll
                         for (int mt = 0; mt < MT; ++mt) {
@@ -390,12 +404,20 @@ __global__ void __launch_bounds__(QMV_THREADS, 1)
                             for (int e = 0; e < 2; ++e) {
                                 const int tok = tb * S::MTOK + 8 * mt + 2 * t + e;
                                 if (tok >= seg_rows) continue;
-                                float v = acc[0][r][mt][2 * h + e];
-                                if constexpr (NMAT == 2) v = swiglu_t<T>(v, acc[1][r][mt][2 * h + e]);
+                                float v = acc[0][mt][2 * h + e];
+                                if constexpr (NMAT == 2) v = swiglu_t<T>(v, acc[1][mt][2 * h + e]);
                                 store_out(a, seg_row0 + tok, n, v, kBF16);
                             }
                         }
                     }
+                }
+                if (a.ks == 1) {
+#pragma unroll
+                    for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                        for (int q = 0; q < MT; ++q)
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) acc[m][q][e] = 0.0f;
                 }
             }
         }
@@ -403,34 +425,30 @@ __global__ void __launch_bounds__(QMV_THREADS, 1)
     if (a.ks == 1) return;
 
     // ------------------ split-K over the cluster (one token block) ------------------
-    if (warp < QMV_CONSUMERS) {
+    if (warp < QMV_CW && kq == 0) {
 #pragma unroll
         for (int m = 0; m < NMAT; ++m)
 #pragma unroll
-            for (int r = 0; r < R; ++r)
+            for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int row = warp * 16 * R + 16 * r + pi_row(g) + 8 * h;
-#pragma unroll
-                    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-                        for (int e = 0; e < 2; ++e)
-                            part[(m * S::BN + row) * S::MTOK + 8 * mt + 2 * t + e] = ok ? acc[m][r][mt][2 * h + e] : 0.0f;
+                for (int e = 0; e < 4; ++e) {
+                    const int row = ra + 8 * (e >> 1), tok = 8 * mt + 2 * t + (e & 1);
+                    part[(m * S::MTOK + tok) * S::BN + row] = ok ? acc[m][mt][e] : 0.0f;
                 }
     }
-    if (!a.grouped) grid_dep_wait();
+    if (warp == QMV_CW && !a.grouped) grid_dep_wait();
     cluster_sync();
     const uint32_t part_local = smem_u32(part);
-    const int nout = S::BN * S::MTOK;
+    constexpr int nout = S::BN * S::MTOK;
     for (int idx = krank * QMV_THREADS + threadIdx.x; idx < nout; idx += a.ks * QMV_THREADS) {
-        const int row = idx / S::MTOK, tok = idx % S::MTOK;
+        const int tok = idx / S::BN, row = idx % S::BN;  // consecutive threads: consecutive output columns
         const int n = n0 + row;
         if (tok >= seg_rows || n >= a.N) continue;
         float v0 = 0.0f, v1 = 0.0f;
         for (int q = 0; q < a.ks; ++q) {
             const uint32_t base = map_peer(part_local, q);
-            v0 += ld_dsmem_f(base + 4 * (row * S::MTOK + tok));
-            if constexpr (NMAT == 2) v1 += ld_dsmem_f(base + 4 * ((S::BN + row) * S::MTOK + tok));
+            v0 += ld_dsmem_f(base + 4 * (tok * S::BN + row));
+            if constexpr (NMAT == 2) v1 += ld_dsmem_f(base + 4 * ((S::MTOK + tok) * S::BN + row));
         }
         if constexpr (NMAT == 2) v0 = swiglu_t<T>(v0, v1);
         store_out(a, seg_row0 + tok, n, v0, kBF16);
@@ -442,21 +460,21 @@ __global__ void __launch_bounds__(QMV_THREADS, 1)
 // host side
 // ------------------------------------------------------------------------------------------------
 
-template <typename T, int BITS, int MT, int R, int NMAT>
+template <typename T, int BITS, int MT, int WK, int NMAT>
 static int qmv_launch_t(const void* x, int x_rows, const QmvMats& mats, QmvArgs a, int ks, int ns_req, int n_seg_grid,
                         cudaStream_t st) {
-    using S = QmvShape<T, BITS, MT, R, NMAT>;
+    using S = QmvShape<T, BITS, MT, WK, NMAT>;
     const DeviceInfo& di = device_info();
     const int K = a.K;
-    a.nchunk = (K + QMV_BK - 1) / QMV_BK;
+    a.nchunk = (K + S::BK - 1) / S::BK;
     if (ks < 1) ks = 1;
     if (ks > a.nchunk) ks = a.nchunk;
     if (ks > 16) ks = 16;
     a.ks = ks;
     const int per_cta = (a.nchunk + ks - 1) / ks;
     // stages: as many as the CTA has chunks, within a budget that lets two CTAs share an SM
-    const size_t fixed = 2 * QMV_MAX_STAGES * 8 + 128 + (ks > 1 ? S::PART_BYTES : 0) + 1024;
-    size_t budget = 110 * 1024;
+    const size_t fixed = 2 * QMV_MAX_STAGES * 8 + S::RED_BYTES + (ks > 1 ? S::PART_BYTES : 0) + 1024;
+    size_t budget = di.smem_per_sm / 2 - 1024;
     if (fixed + S::STAGE_BYTES > budget) budget = di.smem_optin;
     int ns = int((budget - fixed) / S::STAGE_BYTES);
     if (ns < 1) return LQ_E_SHAPE;
@@ -473,7 +491,7 @@ static int qmv_launch_t(const void* x, int x_rows, const QmvMats& mats, QmvArgs 
         const uint64_t rows = uint64_t(mats.rows_total[m]);
         const uint64_t wdims[3] = {32, rows, uint64_t(K) * BITS / 1024};
         const uint64_t wstr[2] = {uint64_t(K) * BITS / 8, 128};
-        const uint32_t wbox[3] = {32, uint32_t(S::BN), uint32_t(S::SEGW)};
+        const uint32_t wbox[3] = {32, uint32_t(S::BN), 2};
         const int rc = make_tmap(&tw[m], CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, mats.w[m], wdims, wstr, wbox,
                                  CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
@@ -492,15 +510,15 @@ static int qmv_launch_t(const void* x, int x_rows, const QmvMats& mats, QmvArgs 
     {
         const uint64_t xdims[3] = {64, uint64_t(x_rows), uint64_t(K / 64)};
         const uint64_t xstr[2] = {uint64_t(K) * 2, 128};
-        const uint32_t xbox[3] = {64, uint32_t(S::MTOK), 8};
+        const uint32_t xbox[3] = {64, uint32_t(S::MTOK), uint32_t(S::BK / 64)};
         const int rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, x, xdims, xstr, xbox,
                                  CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
     }
     const int kg = K / 64;
-    a.sb_vec = (kg % 8 == 0) ? 16 : (kg % 4 == 0) ? 8 : 4;
+    a.sb_vec = (S::SBROW == 16 && kg % 8 == 0) ? 16 : (kg % 4 == 0) ? 8 : 4;
 
-    auto kern = qmv_kernel<T, BITS, MT, R, NMAT>;
+    auto kern = qmv_kernel<T, BITS, MT, WK, NMAT>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return LQ_E_CUDA;
     if (ks > 8) {
@@ -531,27 +549,40 @@ static int qmv_launch_t(const void* x, int x_rows, const QmvMats& mats, QmvArgs 
 }
 
 template <typename T, int BITS, int NMAT>
-static int qmv_dispatch_mt(int MT, int R, const void* x, int x_rows, const QmvMats& mats, const QmvArgs& a, int ks,
+static int qmv_dispatch_mt(int MT, int WK, const void* x, int x_rows, const QmvMats& mats, const QmvArgs& a, int ks,
                            int ns, int n_seg_grid, cudaStream_t st) {
-#define LQ_QMV_CASE(mt, r) \
-    if (MT == mt && R == r) return qmv_launch_t<T, BITS, mt, r, NMAT>(x, x_rows, mats, a, ks, ns, n_seg_grid, st);
+#define LQ_QMV_CASE(mt, wk) \
+    if (MT == mt && WK == wk) return qmv_launch_t<T, BITS, mt, wk, NMAT>(x, x_rows, mats, a, ks, ns, n_seg_grid, st);
     LQ_QMV_CASE(1, 1)
     LQ_QMV_CASE(1, 2)
+    LQ_QMV_CASE(1, 4)
     LQ_QMV_CASE(2, 1)
     LQ_QMV_CASE(2, 2)
+    LQ_QMV_CASE(2, 4)
     LQ_QMV_CASE(4, 1)
+    LQ_QMV_CASE(4, 2)
     LQ_QMV_CASE(8, 1)
+    LQ_QMV_CASE(8, 2)
 #undef LQ_QMV_CASE
     return LQ_E_UNSUPPORTED;
 }
 
-// Default split-K: enough CTAs to cover the SMs about once, limited by the number of 512-wide K chunks
-// and the portable cluster size.
+// Default split-K: the factor (dividing the K chunks evenly when possible) that brings the CTA count
+// closest to two per SM without exceeding it; 1 when a single pass already fills the GPU.
 static int qmv_default_ks(int n_ctas, int nchunk, int sm_count) {
+    const int slots = 2 * sm_count;
     int best = 1;
+    double best_score = -1.0;
     for (int ks = 1; ks <= 8 && ks <= nchunk; ++ks) {
-        best = ks;
-        if (n_ctas * ks >= sm_count) break;
+        const int ctas = n_ctas * ks;
+        if (ctas > slots && ks > 1) break;
+        const double fill = double(ctas) / slots;               // <= 1
+        const double even = (nchunk % ks == 0) ? 1.0 : 0.85;     // uneven K slices leave CTAs idle
+        const double score = fill * even;
+        if (score > best_score) {
+            best_score = score;
+            best = ks;
+        }
     }
     return best;
 }
@@ -565,33 +596,39 @@ bool qmv_shape_ok(int K, int bits) {
 
 int qmv_run(const void* x, int x_rows, const QmvMats& mats, int nmat, QmvArgs a, int bits, int dtype, const int* p,
             int max_seg_rows, int n_seg_grid, cudaStream_t st) {
-    int MT = p ? p[0] : 0, R = p ? p[1] : 0, ks = p ? p[2] : 0, ns = p ? p[3] : 0;
+    int MT = p ? p[0] : 0, WK = p ? p[1] : 0, ks = p ? p[2] : 0, ns = p ? p[3] : 0;
     if (a.M < 1 || max_seg_rows < 1) return LQ_E_SHAPE;
     if (!qmv_shape_ok(a.K, bits)) return LQ_E_SHAPE;
     if (MT == 0) MT = max_seg_rows <= 8 ? 1 : max_seg_rows <= 16 ? 2 : max_seg_rows <= 32 ? 4 : 8;
     if (MT != 1 && MT != 2 && MT != 4 && MT != 8) return LQ_E_ARG;
-    if (R == 0) R = (bits == 8 || nmat == 2 || MT >= 4) ? 1 : 2;
-    if (MT >= 4) R = 1;
-    const int nchunk = (a.K + QMV_BK - 1) / QMV_BK;
+    const int nchunk = (a.K + (2048 / bits) - 1) / (2048 / bits);
+    const int sms = device_info().sm_count;
+    if (WK == 0) {
+        // rows per CTA: 128 (WK=1) unless that leaves the GPU short of CTAs, then 64 / 32
+        WK = 1;
+        const int tiles128 = (a.N + 127) / 128 * n_seg_grid;
+        if (tiles128 * nchunk < sms || (nmat == 2 && bits == 8)) WK = 2;
+        if (MT >= 4 && WK > 2) WK = 2;
+    }
+    if (WK != 1 && WK != 2 && WK != 4) return LQ_E_ARG;
+    const int bn = 16 * (8 / WK);
     const int single_block = max_seg_rows <= 8 * MT;
-    if (ks == 0)
-        ks = single_block ? qmv_default_ks(((a.N + 64 * R - 1) / (64 * R)) * n_seg_grid, nchunk, device_info().sm_count)
-                          : 1;
+    if (ks == 0) ks = single_block ? qmv_default_ks(((a.N + bn - 1) / bn) * n_seg_grid, nchunk, sms) : 1;
     if (!single_block) ks = 1;
     const bool bf16 = dtype == LQ_BF16;
     if (bits == 4) {
         if (nmat == 1)
-            return bf16 ? qmv_dispatch_mt<__nv_bfloat16, 4, 1>(MT, R, x, x_rows, mats, a, ks, ns, n_seg_grid, st)
-                        : qmv_dispatch_mt<__half, 4, 1>(MT, R, x, x_rows, mats, a, ks, ns, n_seg_grid, st);
-        return bf16 ? qmv_dispatch_mt<__nv_bfloat16, 4, 2>(MT, R, x, x_rows, mats, a, ks, ns, n_seg_grid, st)
-                    : qmv_dispatch_mt<__half, 4, 2>(MT, R, x, x_rows, mats, a, ks, ns, n_seg_grid, st);
+            return bf16 ? qmv_dispatch_mt<__nv_bfloat16, 4, 1>(MT, WK, x, x_rows, mats, a, ks, ns, n_seg_grid, st)
+                        : qmv_dispatch_mt<__half, 4, 1>(MT, WK, x, x_rows, mats, a, ks, ns, n_seg_grid, st);
+        return bf16 ? qmv_dispatch_mt<__nv_bfloat16, 4, 2>(MT, WK, x, x_rows, mats, a, ks, ns, n_seg_grid, st)
+                    : qmv_dispatch_mt<__half, 4, 2>(MT, WK, x, x_rows, mats, a, ks, ns, n_seg_grid, st);
     }
     if (bits == 8) {
         if (nmat == 1)
-            return bf16 ? qmv_dispatch_mt<__nv_bfloat16, 8, 1>(MT, R, x, x_rows, mats, a, ks, ns, n_seg_grid, st)
-                        : qmv_dispatch_mt<__half, 8, 1>(MT, R, x, x_rows, mats, a, ks, ns, n_seg_grid, st);
-        return bf16 ? qmv_dispatch_mt<__nv_bfloat16, 8, 2>(MT, R, x, x_rows, mats, a, ks, ns, n_seg_grid, st)
-                    : qmv_dispatch_mt<__half, 8, 2>(MT, R, x, x_rows, mats, a, ks, ns, n_seg_grid, st);
+            return bf16 ? qmv_dispatch_mt<__nv_bfloat16, 8, 1>(MT, WK, x, x_rows, mats, a, ks, ns, n_seg_grid, st)
+                        : qmv_dispatch_mt<__half, 8, 1>(MT, WK, x, x_rows, mats, a, ks, ns, n_seg_grid, st);
+        return bf16 ? qmv_dispatch_mt<__nv_bfloat16, 8, 2>(MT, WK, x, x_rows, mats, a, ks, ns, n_seg_grid, st)
+                    : qmv_dispatch_mt<__half, 8, 2>(MT, WK, x, x_rows, mats, a, ks, ns, n_seg_grid, st);
     }
     return LQ_E_UNSUPPORTED;
 }

@@ -9,7 +9,7 @@ fastest small-M kernel (``_small_matmul`` -> ``_choose`` -> ``_launcher``, local
 ``launch(choice, M, K, N, dtype) -> f(x, w, scales, biases) -> y`` with unchanged MLX tensors -- but
 every path is a hand-written sm_100a kernel of liblq.so:
 
-* ``("qmv", MT, R, KS, NS)`` -- decode family (TMA-staged packed weights, register dequant into
+* ``("qmv", MT, WK, KS, NS)`` -- decode family (TMA-staged packed weights, register dequant into
   mma.sync fragments, cluster split-K), any M (weights streamed once per 64 rows);
 * ``("tc", ...)`` -- prefill family (dequantized tiles in shared memory feeding tcgen05.mma with
   TMEM accumulators), M >= 128.
@@ -100,7 +100,7 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, bia
                      transpose: bool = True, group_size: int = 64, bits: int = 4,
                      choice: Optional[Sequence] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """y = x . dequant(w)^T (mx.quantized_matmul(x, w, scales, biases, transpose=True, group_size, bits))
-    for x (..., K) fp16/bf16. ``choice`` = ("qmv", MT, R, KS, NS) / ("tc", ...) / None (auto)."""
+    for x (..., K) fp16/bf16. ``choice`` = ("qmv", MT, WK, KS, NS) / ("tc", ...) / None (auto)."""
     if not transpose:
         raise NotImplementedError("only transpose=True (the layout of every reference call site)")
     shape = x.shape
@@ -175,15 +175,20 @@ def launch(choice: Sequence, M: int, K: int, N: int, dtype: torch.dtype, bits: i
 
 
 def candidates(M: int, K: int, N: int, bits: int = 4) -> list:
-    """Tuning candidates for one shape (the analogue of locals/kernels.py:654-674)."""
-    out = []
+    """Tuning candidates for one shape (the analogue of locals/kernels.py:654-674): decode tilings
+    ("qmv", MT token tiles of 8, WK warps splitting K per 16-row fragment, KS cluster split-K, NS stages,
+    0 = the library's choice) and, from PREFILL_M rows, the tensor-core GEMM."""
+    out = [("qmv", 0, 0, 0, 0)]
     if M <= MAX_SMALL_M:
-        mts = [mt for mt in (1, 2, 4, 8) if 8 * mt >= min(M, 64)][:2]
-        for mt in mts:
-            for r in ((1, 2) if (mt <= 2 and bits == 4) else (1,)):
-                for ks in (1, 2, 4, 8):
-                    if ks <= max(1, K // 512):
-                        out.append(("qmv", mt, r, ks, 0))
+        bk = 2048 // bits
+        nchunk = max(1, (K + bk - 1) // bk)
+        mt0 = 1 if M <= 8 else 2 if M <= 16 else 4 if M <= 32 else 8
+        for wk in (1, 2, 4):
+            if mt0 >= 4 and wk > 2:
+                continue
+            for ks in (1, 2, 3, 4, 5, 8):
+                if ks <= nchunk:
+                    out.append(("qmv", mt0, wk, ks, 0))
     if M >= PREFILL_M:
         out.append(("tc",))
     return out
