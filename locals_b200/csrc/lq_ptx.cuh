@@ -155,7 +155,9 @@ __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
 
 __device__ __forceinline__ float ld_dsmem_f(uint32_t addr) {
     float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    // no "memory" clobber: independent remote loads may be in flight together (ordering against the
+    // producers' writes comes from the cluster barrier before them)
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
     return v;
 }
 

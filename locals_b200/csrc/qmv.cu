@@ -310,20 +310,31 @@ __global__ void __launch_bounds__(QMV_THREADS, (MT * NMAT <= 2) ? 2 : 1)
                     tma_load_3d(smem + s * S::STAGE_BYTES + m * S::W_BYTES, tw[m], &full[s], 0,
                                 wrow0 + n0 + a.row_off[m], c * 2, pol_w);
             }
-            // scales and biases: per matrix 2 arrays x BN rows x SBROW bytes
-            const int per_mat = 2 * S::BN * units_row;
-            for (int u = lane; u < NMAT * per_mat; u += 32) {
-                const int m = u / per_mat, rem = u % per_mat;
-                const int arr = rem / (S::BN * units_row);
-                const int r = (rem / units_row) % S::BN, part_i = rem % units_row;
-                const int grow = wrow0 + n0 + a.row_off[m] + r;
-                const int gcol = c * S::GPS + part_i * (vb / 2);  // first group of this unit
-                const bool valid = grow < a.rows_total[m] && gcol < kg;
-                const uint8_t* base = reinterpret_cast<const uint8_t*>(arr ? a.bptr[m] : a.sptr[m]);
-                const uint8_t* src = valid ? base + (size_t(grow) * kg + gcol) * 2 : base;
-                const uint32_t dst = st + NMAT * S::W_BYTES + S::X_BYTES + (2 * m + arr) * S::SB_BYTES +
-                                     r * S::SBROW + part_i * vb;
-                cp_async(dst, src, vb, valid);
+            // scales and biases: per matrix 2 arrays x BN rows x SBROW bytes, lane-strided rows, no divisions
+            const uint32_t sb_dst = st + NMAT * S::W_BYTES + S::X_BYTES;
+            const int gcol0 = c * S::GPS;
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) {
+                const int row0 = wrow0 + n0 + a.row_off[m];
+                const uint8_t* sbase = reinterpret_cast<const uint8_t*>(a.sptr[m]);
+                const uint8_t* bbase = reinterpret_cast<const uint8_t*>(a.bptr[m]);
+#pragma unroll
+                for (int rr = 0; rr < S::BN; rr += 32) {
+                    const int r = rr + lane;
+                    const int grow = row0 + r;
+                    const bool row_ok = (r < S::BN) && grow < a.rows_total[m];
+                    const size_t roff = size_t(grow) * kg;
+                    for (int part_i = 0; part_i < units_row; ++part_i) {
+                        const int gcol = gcol0 + part_i * (vb >> 1);
+                        const bool valid = row_ok && gcol < kg;
+                        const size_t off = valid ? (roff + gcol) * 2 : 0;
+                        const uint32_t d = sb_dst + 2 * m * S::SB_BYTES + r * S::SBROW + part_i * vb;
+                        if (r < S::BN) {
+                            cp_async(d, sbase + off, vb, valid);
+                            cp_async(d + S::SB_BYTES, bbase + off, vb, valid);
+                        }
+                    }
+                }
             }
             cp_async_arrive(&full[s]);
         };
@@ -439,16 +450,26 @@ __global__ void __launch_bounds__(QMV_THREADS, (MT * NMAT <= 2) ? 2 : 1)
     if (warp == QMV_CW && !a.grouped) grid_dep_wait();
     cluster_sync();
     const uint32_t part_local = smem_u32(part);
+    uint32_t peer[16];
+#pragma unroll
+    for (int q = 0; q < 16; ++q) peer[q] = q < a.ks ? map_peer(part_local, q) : part_local;
     constexpr int nout = S::BN * S::MTOK;
     for (int idx = krank * QMV_THREADS + threadIdx.x; idx < nout; idx += a.ks * QMV_THREADS) {
         const int tok = idx / S::BN, row = idx % S::BN;  // consecutive threads: consecutive output columns
         const int n = n0 + row;
         if (tok >= seg_rows || n >= a.N) continue;
+        // every peer's partial is requested before any is summed (one round of remote latency)
+        float v[16], u[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+            v[q] = q < a.ks ? ld_dsmem_f(peer[q] + 4 * (tok * S::BN + row)) : 0.0f;
+            if constexpr (NMAT == 2) u[q] = q < a.ks ? ld_dsmem_f(peer[q] + 4 * ((S::MTOK + tok) * S::BN + row)) : 0.0f;
+        }
         float v0 = 0.0f, v1 = 0.0f;
-        for (int q = 0; q < a.ks; ++q) {
-            const uint32_t base = map_peer(part_local, q);
-            v0 += ld_dsmem_f(base + 4 * (tok * S::BN + row));
-            if constexpr (NMAT == 2) v1 += ld_dsmem_f(base + 4 * ((S::MTOK + tok) * S::BN + row));
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+            v0 += v[q];
+            if constexpr (NMAT == 2) v1 += u[q];
         }
         if constexpr (NMAT == 2) v0 = swiglu_t<T>(v0, v1);
         store_out(a, seg_row0 + tok, n, v0, kBF16);
@@ -567,18 +588,20 @@ static int qmv_dispatch_mt(int MT, int WK, const void* x, int x_rows, const QmvM
     return LQ_E_UNSUPPORTED;
 }
 
-// Default split-K: the factor (dividing the K chunks evenly when possible) that brings the CTA count
-// closest to two per SM without exceeding it; 1 when a single pass already fills the GPU.
+// Default split-K for a grid of n_ctas row tiles: the factor (dividing the K chunks evenly when possible)
+// that brings the CTA count closest to one per SM without exceeding it. One CTA per SM leaves the other
+// half of every SM free for the NEXT kernel's CTA, which (programmatic dependent launch) prefetches its
+// weights into shared memory while this kernel computes.
 static int qmv_default_ks(int n_ctas, int nchunk, int sm_count) {
-    const int slots = 2 * sm_count;
     int best = 1;
     double best_score = -1.0;
     for (int ks = 1; ks <= 8 && ks <= nchunk; ++ks) {
         const int ctas = n_ctas * ks;
-        if (ctas > slots && ks > 1) break;
-        const double fill = double(ctas) / slots;               // <= 1
-        const double even = (nchunk % ks == 0) ? 1.0 : 0.85;     // uneven K slices leave CTAs idle
-        const double score = fill * even;
+        if (ctas > sm_count && ks > 1) break;
+        const int per = (nchunk + ks - 1) / ks;
+        const double fill = double(ctas) / sm_count;                        // <= 1
+        const double balance = double(nchunk) / (double(per) * ks);         // uneven K slices idle some CTAs
+        const double score = (fill > 1.0 ? 1.0 / fill : fill) * balance;
         if (score > best_score) {
             best_score = score;
             best = ks;
@@ -604,13 +627,14 @@ int qmv_run(const void* x, int x_rows, const QmvMats& mats, int nmat, QmvArgs a,
     const int nchunk = (a.K + (2048 / bits) - 1) / (2048 / bits);
     const int sms = device_info().sm_count;
     if (WK == 0) {
-        // rows per CTA: 128 (WK=1) unless that leaves the GPU short of CTAs, then 64 / 32
+        // rows per CTA: 128 (WK=1), or 64 / 32 when 128-row tiles leave SMs idle even with split-K
         WK = 1;
         const int tiles128 = (a.N + 127) / 128 * n_seg_grid;
-        if (tiles128 * nchunk < sms || (nmat == 2 && bits == 8)) WK = 2;
-        if (MT >= 4 && WK > 2) WK = 2;
+        if (tiles128 * nchunk < sms) WK = 2;
+        const int tiles64 = (a.N + 63) / 64 * n_seg_grid;
+        if (WK == 2 && tiles64 * nchunk < sms / 2 && MT <= 2) WK = 4;
+        if (nmat == 2 && bits == 8 && WK == 1) WK = 2;  // two 8-bit matrices: keep a stage within half an SM
     }
-    if (WK != 1 && WK != 2 && WK != 4) return LQ_E_ARG;
     const int bn = 16 * (8 / WK);
     const int single_block = max_seg_rows <= 8 * MT;
     if (ks == 0) ks = single_block ? qmv_default_ks(((a.N + bn - 1) / bn) * n_seg_grid, nchunk, sms) : 1;
