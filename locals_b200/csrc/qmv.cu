@@ -588,20 +588,19 @@ static int qmv_dispatch_mt(int MT, int WK, const void* x, int x_rows, const QmvM
     return LQ_E_UNSUPPORTED;
 }
 
-// Default split-K for a grid of n_ctas row tiles: the factor (dividing the K chunks evenly when possible)
-// that brings the CTA count closest to one per SM without exceeding it. One CTA per SM leaves the other
-// half of every SM free for the NEXT kernel's CTA, which (programmatic dependent launch) prefetches its
-// weights into shared memory while this kernel computes.
+// Default split-K for a grid of n_ctas row tiles: the largest factor that keeps the CTA count within
+// 1.25 per SM (measured on B200: more CTAs than that only queue), preferring factors that split the K
+// chunks evenly.
 static int qmv_default_ks(int n_ctas, int nchunk, int sm_count) {
     int best = 1;
     double best_score = -1.0;
+    const double cap = 1.25 * sm_count;
     for (int ks = 1; ks <= 8 && ks <= nchunk; ++ks) {
         const int ctas = n_ctas * ks;
-        if (ctas > sm_count && ks > 1) break;
+        if (ks > 1 && ctas > cap) break;
         const int per = (nchunk + ks - 1) / ks;
-        const double fill = double(ctas) / sm_count;                        // <= 1
-        const double balance = double(nchunk) / (double(per) * ks);         // uneven K slices idle some CTAs
-        const double score = (fill > 1.0 ? 1.0 / fill : fill) * balance;
+        const double balance = double(nchunk) / (double(per) * ks);  // uneven K slices idle some CTAs
+        const double score = double(ctas) * balance;
         if (score > best_score) {
             best_score = score;
             best = ks;
@@ -627,13 +626,10 @@ int qmv_run(const void* x, int x_rows, const QmvMats& mats, int nmat, QmvArgs a,
     const int nchunk = (a.K + (2048 / bits) - 1) / (2048 / bits);
     const int sms = device_info().sm_count;
     if (WK == 0) {
-        // rows per CTA: 128 (WK=1), or 64 / 32 when 128-row tiles leave SMs idle even with split-K
-        WK = 1;
-        const int tiles128 = (a.N + 127) / 128 * n_seg_grid;
-        if (tiles128 * nchunk < sms) WK = 2;
-        const int tiles64 = (a.N + 63) / 64 * n_seg_grid;
-        if (WK == 2 && tiles64 * nchunk < sms / 2 && MT <= 2) WK = 4;
-        if (nmat == 2 && bits == 8 && WK == 1) WK = 2;  // two 8-bit matrices: keep a stage within half an SM
+        // 64-row CTAs (two warps per 16-row fragment, each taking half of every stage): the measured best
+        // for M <= 16 on B200, where the dequantizing warps, not the loads, bound the kernel
+        WK = 2;
+        if (MT >= 8) WK = 2;
     }
     const int bn = 16 * (8 / WK);
     const int single_block = max_seg_rows <= 8 * MT;
