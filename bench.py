@@ -357,6 +357,71 @@ def bench_prefill(torch, steps, warmup, dev, stream):
     return {"tflops": 2 * 2048 * 14336 * 4096 / (ms * 1e-3) / 1e12, "ms": ms}
 
 
+
+# --------------------------------------------------------------------------------------------------
+# sharded configurations (all ranks; NCCL collectives; each rank's time on its own stream, max over ranks)
+# --------------------------------------------------------------------------------------------------
+
+def _timed_max(torch, fn, steps, warmup, stream, dist):
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = timed(torch, fn, steps, 0, stream)
+    t = torch.tensor([ms], device=torch.device("cuda", torch.cuda.current_device()))
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t[0])
+
+
+def bench_sharded(torch, dist, ws, steps, warmup, dev, stream):
+    """Configs 3, 4, 5 split over the ranks as BASELINE describes (column shards + all-gather, experts +
+    all-to-all). Eager launches (collectives between kernels); returns rank-0 results."""
+    from locals_b200 import moe
+    from locals_b200.kernels import QuantizedLinear
+    from locals_b200.shard import ExpertParallelMoE, ShardedMLP, ColumnShardedLinear
+
+    out = {}
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2)
+    g_ = QuantizedLinear(*make_layer(torch, 9728, 2560, 8, torch.bfloat16, gen, dev), bits=8)
+    u_ = QuantizedLinear(*make_layer(torch, 9728, 2560, 8, torch.bfloat16, gen, dev), bits=8)
+    d_ = QuantizedLinear(*make_layer(torch, 2560, 9728, 8, torch.bfloat16, gen, dev), bits=8)
+    mlp = ShardedMLP(g_, u_, d_)
+    del g_, u_, d_
+    out["cfg3_mlp_8bit_sharded"] = {}
+    for M in (1, 16, 64):
+        x = torch.randn((M, 2560), generator=gen, device=dev).to(torch.bfloat16)
+        ms = _timed_max(torch, lambda: mlp(x), steps, warmup, stream, dist)
+        out["cfg3_mlp_8bit_sharded"][f"M={M}"] = {"us_per_mlp": round(ms * 1e3, 2), "tok/s": round(M / (ms * 1e-3), 1)}
+    del mlp
+    gen.manual_seed(3)
+    E, D, I = 64, 2048, 768
+
+    def stack(N, Kd):
+        ws_ = [make_layer(torch, N, Kd, 4, torch.bfloat16, gen, dev) for _ in range(E)]
+        return tuple(torch.stack([w[i] for w in ws_]).contiguous() for i in range(3))
+
+    gate, up, down = stack(I, D), stack(I, D), stack(D, I)
+    wr = (torch.randn((E, D), generator=gen, device=dev) * 0.02).to(torch.float16)
+    ep = ExpertParallelMoE(wr, gate, up, down, top_k=4)
+    del gate, up, down
+    out["cfg4_moe_ep"] = {}
+    for M in (8, 64, 512):
+        if M % ws:
+            continue
+        x = torch.randn((M // ws, D), generator=gen, device=dev).to(torch.bfloat16)
+        ms = _timed_max(torch, lambda: ep(x), steps, warmup, stream, dist)
+        out["cfg4_moe_ep"][f"M={M}"] = {"us_per_layer": round(ms * 1e3, 2), "tok/s": round(M / (ms * 1e-3), 1)}
+    del ep
+    gen.manual_seed(4)
+    lin = ColumnShardedLinear(QuantizedLinear(*make_layer(torch, 14336, 4096, 4, torch.bfloat16, gen, dev)))
+    x = torch.randn((2048, 4096), generator=gen, device=dev).to(torch.bfloat16)
+    ms = _timed_max(torch, lambda: lin(x), max(3, steps // 4), warmup, stream, dist)
+    out["cfg5_prefill_sharded"] = {"ms": round(ms, 3), "TFLOP/s": round(2 * 2048 * 14336 * 4096 / (ms * 1e-3) / 1e12, 1)}
+    return out
+
+
 def run_gpu(args):
     import torch
 
@@ -424,6 +489,9 @@ def run_gpu(args):
         extra["cfg5_prefill"] = {"TFLOP/s": round(r["tflops"], 1), "frac_bf16": round(r["tflops"] / tfl, 3),
                                  "ms": round(r["ms"], 3)}
 
+    if ws > 1 and not args.quick:
+        extra.update(bench_sharded(torch, dist, ws, max(5, args.steps // 2), args.warmup, dev, stream))
+
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
         gbs, threads, sample = cpu_qkv_sample(seconds=10.0)
@@ -439,7 +507,8 @@ def run_gpu(args):
                                    "W 4-bit g64 [6144,2560] -> q[16,32,128] k,v[16,8,128]",
                        "layers_per_step": head_layers, "weights_per_step_MB": round(head["bytes_per_step"] / 1e6, 1),
                        "l2": "inputs larger than L2 (distinct weights per layer, 318 MB per step)",
-                       "parallelism": f"{ws} independent replicas (weak)" if ws > 1 else "1 GPU",
+                       "parallelism": (f"{ws} replicas of the config-2 layer stack (weak); configs 3-5 sharded "
+                                       "with NCCL in the cfg*_sharded / cfg4_moe_ep keys") if ws > 1 else "1 GPU",
                        "graph": "CUDA graph of the step, PDL between launches"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "traffic": traffic,

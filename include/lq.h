@@ -105,7 +105,8 @@ int lq_moe_gather(const void* x, const int32_t* order, int P, int k, int D, void
  *           gate = (w0, s0, b0), up = (w1, s1, b1), each stacked (E, N, K*bits/32) / (E, N, K/group).
  * glu == 0: out (P, N) = xs . w0_e^T.
  * max_rows bounds the rows of one segment (the token count of the step: a token names an expert at
- * most once). out in dtype, rows in pair order. */
+ * most once). out in dtype, rows in pair order. Rows grouped under expert id E (group with E + 1
+ * buckets) are padding: they are skipped and their output rows left unwritten. */
 int lq_moe_experts(const void* xs, const int32_t* starts, const int32_t* experts, const int32_t* nseg, int P,
                    int max_rows, int glu, const uint32_t* w0, const void* s0, const void* b0, const uint32_t* w1,
                    const void* s1, const void* b1, void* out, int E, int N, int K, int bits, int group_size, int dtype,

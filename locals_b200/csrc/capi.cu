@@ -253,7 +253,7 @@ int lq_moe_experts(const void* xs, const int32_t* starts, const int32_t* experts
     m.s[1] = glu ? s1 : s0;
     m.b[1] = glu ? b1 : b0;
     m.rows_total[0] = m.rows_total[1] = E * N;
-    const int nseg_grid = E < P ? E : P;
+    const int nseg_grid = (E + 1) < P ? (E + 1) : P;  // (one more for a padding bucket, expert id E)
     return finish(qmv_run(xs, P, m, glu ? 2 : 1, a, bits, dtype, nullptr, max_rows, nseg_grid,
                           reinterpret_cast<cudaStream_t>(stream)));
 }

@@ -256,7 +256,8 @@ __global__ void __launch_bounds__(QMV_THREADS, (MT * NMAT <= 2) ? 2 : 1)
         seg_row0 = a.starts[sgi];
         seg_rows = a.starts[sgi + 1] - seg_row0;
         const int e = a.experts[sgi];
-        if (e < 0 || e >= a.n_experts || seg_rows < 0) {
+        if (e == a.n_experts) return;  // the padding bucket: rows nobody asked for, left unwritten
+        if (e < 0 || e > a.n_experts || seg_rows < 0) {
             record_status(LQ_DEV_BOUNDS);
             return;
         }

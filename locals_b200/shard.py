@@ -1,0 +1,220 @@
+"""Multi-GPU sharding of the quantized-matmul path (one process per GPU, torch.distributed over NCCL).
+
+The reference runs one model on one Apple GPU (no distributed code, SURVEY: "collective call sites: none");
+the partitioning here is the one BASELINE's north star asks for:
+
+* ``ColumnShardedLinear`` -- a quantized linear split by output rows (columns of y): rank r keeps rows
+  [r N/G, (r+1) N/G) of the packed weights, scales and biases (quantization groups run along K, so each
+  row block is itself a valid MLX-format matrix, the argument of locals/fuse.py:3-6), computes its slice
+  of y with the decode or prefill kernel and NCCL all-gathers the slices.
+* ``ShardedQKV`` -- the fused q/k/v projection split at head boundaries: rank r keeps H/G query heads and
+  KVH/G key/value heads; its local q/k/v come out of one kernel, then are all-gathered into full q, k, v.
+* ``ShardedMLP`` -- gate||up split by intermediate rows (the SwiGLU is row-local), h all-gathered, the down
+  projection split by output rows, y all-gathered.
+* ``ExpertParallelMoE`` -- E/G experts and M/G tokens per rank. Each rank routes its own tokens, packs the
+  (token, slot) pairs into fixed-capacity per-destination blocks (capacity = its pairs, so no host
+  synchronisation and the step stays capturable in a CUDA graph), NCCL all-to-all dispatches rows and
+  expert ids, the owner runs the grouped expert kernels on what it received, a second all-to-all returns
+  the rows, and the source rank combines each token's slots in slot order (float32).
+
+Every collective is issued by every rank in the same order. Compute goes through liblq.so kernels; the
+``ops`` hook exists so CPU tests can check the partitioning and the collectives with gloo ranks.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, Optional, Sequence
+
+import torch
+import torch.distributed as dist
+
+from .kernels import QuantizedLinear
+
+
+def _world(group) -> tuple:
+    if not dist.is_available() or not dist.is_initialized():
+        return 1, 0
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+@dataclass
+class Ops:
+    """Compute hooks: quantized matmul, SwiGLU matmul, and the MoE stages on one rank's data."""
+
+    qmm: Callable          # (x, (w, s, b), bits) -> y
+    glu: Callable          # (x, gate, up, bits) -> h
+    route: Callable        # (x, router_w, k, mode) -> (inds int32 (T, k), weights f32 (T, k))
+    experts: Callable      # (rows, local_ids, gate, up, down, bits, max_rows) -> out rows (pair order as given)
+    combine: Callable      # (ys (T*k, D) in pair order, weights (T, k)) -> y (T, D), float32 sum in slot order
+
+
+def kernel_ops() -> Ops:
+    from . import kernels, moe
+
+    def qmm(x, q, bits):
+        return kernels.quantized_matmul(x, q[0], q[1], q[2], bits=bits)
+
+    def glu(x, gate, up, bits):
+        return kernels.qmm_glu(x, gate, up, bits=bits)
+
+    def route(x, wr, k, mode):
+        return moe.route_topk(moe.router_logits(x, wr), k, mode)
+
+    def experts(rows, ids, gate, up, down, bits, max_rows):
+        # rows (P, D) with local expert ids (P,) in [0, E) or -1 for padding; padding goes to bucket E,
+        # which the grouped kernel skips (its output rows stay unwritten and are masked by the caller)
+        E = gate[0].shape[0]
+        ids_c = torch.where(ids < 0, torch.full_like(ids, E), ids).to(torch.int32)
+        grouping = moe.group(ids_c, E + 1)
+        order, pos = grouping[0], grouping[4]
+        xs = moe.gather(rows, order, 1)
+        h = moe.experts(xs, grouping, [gate, up], gate[0].shape[1], max_rows=max_rows, bits=bits)
+        ys = moe.experts(h, grouping, [down], down[0].shape[1], max_rows=max_rows, bits=bits)
+        return ys.index_select(0, pos.long())
+
+    def combine(ys, wts):
+        return moe.combine(ys.contiguous(), wts.contiguous(), None)
+
+    return Ops(qmm, glu, route, experts, combine)
+
+
+def _split_rows(t: torch.Tensor, parts: int, idx: int) -> torch.Tensor:
+    n = t.shape[0]
+    if n % parts:
+        raise ValueError(f"{n} rows do not split into {parts} equal shards")
+    step = n // parts
+    return t[idx * step:(idx + 1) * step].contiguous()
+
+
+def all_gather_cols(y_local: torch.Tensor, group=None) -> torch.Tensor:
+    """(M, N/G) slices of every rank -> (M, N), rank r's slice at columns [r N/G, (r+1) N/G)."""
+    G, _ = _world(group)
+    if G == 1:
+        return y_local
+    M, Nl = y_local.shape
+    buf = torch.empty((G * M, Nl), dtype=y_local.dtype, device=y_local.device)  # ranks stacked along dim 0
+    dist.all_gather_into_tensor(buf, y_local.contiguous(), group=group)
+    return buf.view(G, M, Nl).permute(1, 0, 2).reshape(M, G * Nl)
+
+
+class ColumnShardedLinear:
+    def __init__(self, full: QuantizedLinear, group=None, ops: Optional[Ops] = None):
+        self.group = group
+        G, r = _world(group)
+        self.G, self.rank = G, r
+        self.local = QuantizedLinear(_split_rows(full.weight, G, r), _split_rows(full.scales, G, r),
+                                     _split_rows(full.biases, G, r), full.bits, full.group_size)
+        self.ops = ops or kernel_ops()
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        x2 = x.reshape(-1, x.shape[-1])
+        y = self.ops.qmm(x2, (self.local.weight, self.local.scales, self.local.biases), self.local.bits)
+        return all_gather_cols(y, self.group).reshape(*x.shape[:-1], -1)
+
+
+class ShardedQKV:
+    """q/k/v projection split at head boundaries; returns full q (M, H, D), k, v (M, KVH, D)."""
+
+    def __init__(self, q: QuantizedLinear, k: QuantizedLinear, v: QuantizedLinear, n_heads: int, n_kv_heads: int,
+                 head_dim: int, group=None, ops: Optional[Ops] = None, gather: bool = True):
+        G, r = _world(group)
+        if n_heads % G or n_kv_heads % G:
+            raise ValueError("heads do not split evenly over the ranks")
+        self.G, self.rank, self.group, self.gather = G, r, group, gather
+        self.H, self.KVH, self.D = n_heads, n_kv_heads, head_dim
+        parts = [(m, G, r) for m in (q, k, v)]
+        self.w = torch.cat([_split_rows(m.weight, g, i) for m, g, i in parts], 0)
+        self.s = torch.cat([_split_rows(m.scales, g, i) for m, g, i in parts], 0)
+        self.b = torch.cat([_split_rows(m.biases, g, i) for m, g, i in parts], 0)
+        self.bits = q.bits
+        self.widths = (n_heads // G * head_dim, n_kv_heads // G * head_dim, n_kv_heads // G * head_dim)
+        self.ops = ops
+
+    def __call__(self, x: torch.Tensor):
+        x2 = x.reshape(-1, x.shape[-1])
+        M = x2.shape[0]
+        if self.ops is None:
+            from . import kernels
+
+            ql, kl, vl = kernels.qmm_split(x2, self.w, self.s, self.b, self.widths, bits=self.bits)
+        else:
+            y = self.ops.qmm(x2, (self.w, self.s, self.b), self.bits)
+            ql, kl, vl = torch.split(y, list(self.widths), dim=1)
+        if not self.gather:
+            return (ql.reshape(M, self.H // self.G, self.D), kl.reshape(M, self.KVH // self.G, self.D),
+                    vl.reshape(M, self.KVH // self.G, self.D))
+        q = all_gather_cols(ql.contiguous(), self.group).reshape(M, self.H, self.D)
+        k = all_gather_cols(kl.contiguous(), self.group).reshape(M, self.KVH, self.D)
+        v = all_gather_cols(vl.contiguous(), self.group).reshape(M, self.KVH, self.D)
+        return q, k, v
+
+
+class ShardedMLP:
+    """down(swiglu(gate x, up x)) with gate/up split by intermediate rows and down by output rows."""
+
+    def __init__(self, gate: QuantizedLinear, up: QuantizedLinear, down: QuantizedLinear, group=None,
+                 ops: Optional[Ops] = None):
+        G, r = _world(group)
+        self.G, self.rank, self.group = G, r, group
+        self.gate = tuple(_split_rows(t, G, r) for t in (gate.weight, gate.scales, gate.biases))
+        self.up = tuple(_split_rows(t, G, r) for t in (up.weight, up.scales, up.biases))
+        self.down = tuple(_split_rows(t, G, r) for t in (down.weight, down.scales, down.biases))
+        self.bits = gate.bits
+        self.ops = ops or kernel_ops()
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        x2 = x.reshape(-1, x.shape[-1])
+        h = all_gather_cols(self.ops.glu(x2, self.gate, self.up, self.bits), self.group)
+        y = all_gather_cols(self.ops.qmm(h, self.down, self.bits), self.group)
+        return y.reshape(*x.shape[:-1], -1)
+
+
+class ExpertParallelMoE:
+    """Routed MoE with E/G experts and M/G tokens per rank, NCCL all-to-all dispatch and combine."""
+
+    def __init__(self, router_w: torch.Tensor, gate, up, down, top_k: int, mode: int = 0, bits: int = 4,
+                 group=None, ops: Optional[Ops] = None):
+        G, r = _world(group)
+        E = gate[0].shape[0]
+        if E % G:
+            raise ValueError("experts do not split evenly over the ranks")
+        self.G, self.rank, self.group = G, r, group
+        self.E, self.EL = E, E // G
+        self.router_w, self.k, self.mode, self.bits = router_w, top_k, mode, bits
+        self.gate = tuple(_split_rows(t, G, r) for t in gate)
+        self.up = tuple(_split_rows(t, G, r) for t in up)
+        self.down = tuple(_split_rows(t, G, r) for t in down)
+        self.ops = ops or kernel_ops()
+
+    def _a2a(self, t: torch.Tensor) -> torch.Tensor:
+        if self.G == 1:
+            return t
+        out = torch.empty_like(t)
+        dist.all_to_all_single(out, t, group=self.group)
+        return out
+
+    def __call__(self, x_local: torch.Tensor) -> torch.Tensor:
+        """x_local: this rank's tokens (T, D) -> their MoE outputs (T, D)."""
+        T, D = x_local.shape
+        k, G, EL = self.k, self.G, self.EL
+        inds, wts = self.ops.route(x_local, self.router_w, k, self.mode)
+        P = T * k
+        C = P  # capacity per destination: every pair could go to one rank
+        flat = inds.reshape(-1).long()
+        dest = flat // EL
+        # position of each pair inside its destination block: pairs before it with the same destination
+        onehot = torch.nn.functional.one_hot(dest, G).to(torch.int32)           # (P, G)
+        rank_in_dest = (torch.cumsum(onehot, 0) - onehot).gather(1, dest[:, None])[:, 0].long()
+        slot = dest * C + rank_in_dest                                          # row in the send buffer
+        send_x = torch.zeros((G * C, D), dtype=x_local.dtype, device=x_local.device)
+        send_x.index_copy_(0, slot, x_local.index_select(0, torch.arange(P, device=x_local.device) // k))
+        send_id = torch.full((G * C,), -1, dtype=torch.int32, device=x_local.device)
+        send_id.index_copy_(0, slot, (flat - dest * EL).to(torch.int32))
+        recv_x = self._a2a(send_x)
+        recv_id = self._a2a(send_id)
+        out = self.ops.experts(recv_x, recv_id, self.gate, self.up, self.down, self.bits, max_rows=G * C)
+        out = torch.where((recv_id >= 0)[:, None], out, torch.zeros_like(out))
+        back = self._a2a(out.contiguous())
+        ys = back.index_select(0, slot)                                          # (P, D), pair order
+        return self.ops.combine(ys, wts)

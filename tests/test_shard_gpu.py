@@ -1,0 +1,87 @@
+"""The sharded modules on 2 GPUs with NCCL (skipped when fewer than 2 GPUs are visible): each sharded
+result is compared with the same computation on one GPU."""
+
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, path):
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        from locals_b200 import kernels, moe
+        from locals_b200.kernels import QuantizedLinear
+        from locals_b200.shard import ColumnShardedLinear, ExpertParallelMoE, ShardedMLP
+
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(0)
+
+        def layer(N, K, bits):
+            return kernels.quantize(torch.randn((N, K), generator=gen, device=dev) * 0.02, 64, bits,
+                                    dtype=torch.bfloat16)
+
+        errs = {}
+        lin = QuantizedLinear(*layer(1024, 2048, 4))
+        x = torch.randn((8, 2048), generator=gen, device=dev).to(torch.bfloat16)
+        ref = kernels.quantized_matmul(x, lin.weight, lin.scales, lin.biases)
+        errs["linear"] = float((ColumnShardedLinear(lin)(x).float() - ref.float()).abs().max() / ref.float().abs().max())
+        g, u, d = (QuantizedLinear(*layer(1024, 2048, 8), bits=8), QuantizedLinear(*layer(1024, 2048, 8), bits=8),
+                   QuantizedLinear(*layer(2048, 1024, 8), bits=8))
+        h = kernels.qmm_glu(x, (g.weight, g.scales, g.biases), (u.weight, u.scales, u.biases), bits=8)
+        ref = kernels.quantized_matmul(h, d.weight, d.scales, d.biases, bits=8)
+        errs["mlp"] = float((ShardedMLP(g, u, d)(x).float() - ref.float()).abs().max() / ref.float().abs().max())
+        E, D, I = 16, 1024, 512
+
+        def stack(N, Kd):
+            parts = [layer(N, Kd, 4) for _ in range(E)]
+            return tuple(torch.stack([p[i] for p in parts]).contiguous() for i in range(3))
+
+        gate, up, down = stack(I, D), stack(I, D), stack(D, I)
+        wr = (torch.randn((E, D), generator=gen, device=dev) * 0.05).to(torch.float16)
+        xt = torch.randn((2 * 8, D), generator=gen, device=dev).to(torch.bfloat16)
+        full = moe.MoELayer(wr, gate, up, down, top_k=4)(xt)
+        mine = xt[rank * 8:(rank + 1) * 8].contiguous()
+        got = ExpertParallelMoE(wr, gate, up, down, top_k=4)(mine)
+        ref = full[rank * 8:(rank + 1) * 8]
+        errs["moe"] = float((got.float() - ref.float()).abs().max() / ref.float().abs().max())
+        torch.cuda.synchronize()
+        errs["status"] = kernels.device_status()
+        out = [None] * world
+        dist.all_gather_object(out, errs)
+        if rank == 0:
+            torch.save(out, path)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_two_gpus(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    path = str(tmp_path / "errs.pt")
+    mp.spawn(_worker, args=(2, _port(), path), nprocs=2, join=True)
+    for errs in torch.load(path):
+        assert errs.pop("status") == 0
+        for name, e in errs.items():
+            assert e <= 1e-2, (name, e)
