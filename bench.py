@@ -363,12 +363,20 @@ def bench_prefill(torch, steps, warmup, dev, stream):
 # --------------------------------------------------------------------------------------------------
 
 def _timed_max(torch, fn, steps, warmup, stream, dist):
+    """The step captured in a CUDA graph (NCCL collectives included, after an eager warm-up that sets up
+    the communicator), timed on this rank's stream; the max over ranks. The graph is released here."""
     with torch.cuda.stream(stream):
         for _ in range(warmup):
             fn()
     torch.cuda.synchronize()
     dist.barrier()
-    ms = timed(torch, fn, steps, 0, stream)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = timed(torch, g.replay, steps, 2, stream)
+    del g
     t = torch.tensor([ms], device=torch.device("cuda", torch.cuda.current_device()))
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t[0])
@@ -376,7 +384,7 @@ def _timed_max(torch, fn, steps, warmup, stream, dist):
 
 def bench_sharded(torch, dist, ws, steps, warmup, dev, stream):
     """Configs 3, 4, 5 split over the ranks as BASELINE describes (column shards + all-gather, experts +
-    all-to-all). Eager launches (collectives between kernels); returns rank-0 results."""
+    all-to-all), each step captured in a CUDA graph with its NCCL collectives; returns rank-0 results."""
     from locals_b200 import moe
     from locals_b200.kernels import QuantizedLinear
     from locals_b200.shard import ExpertParallelMoE, ShardedMLP, ColumnShardedLinear
@@ -528,6 +536,69 @@ def run_gpu(args):
     return 0
 
 
+# --------------------------------------------------------------------------------------------------
+# single small cases for ncu captures (--case NAME): a few launches of one kernel family, nothing timed
+# --------------------------------------------------------------------------------------------------
+
+CASES = {
+    "qkv16": "fused QKV decode, x bf16 [16,2560] . 4-bit [6144,2560]^T, 8 distinct layers (72 MB)",
+    "qkv16_l2": "fused QKV decode over 24 layers (218 MB > L2), for DRAM figures",
+    "mlp64": "8-bit MLP gate||up + SiLU.mul and down at M=64, 4 layers",
+    "tc": "prefill GEMM x bf16 [1024,4096] . 4-bit [7168,4096]^T",
+    "moe16": "MoE layer, 64 experts top-4, D 2048, I 768, M=16",
+}
+
+
+def run_case(name):
+    import torch
+
+    from locals_b200 import _lib, kernels, moe
+    from locals_b200.fuse import FusedMLP
+    from locals_b200.kernels import QuantizedLinear
+
+    _lib.lib()
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    if name in ("qkv16", "qkv16_l2"):
+        L = 8 if name == "qkv16" else 24
+        Ws = [make_layer(torch, HEAD_N, HEAD_K, 4, torch.bfloat16, gen, dev) for _ in range(L)]
+        x = torch.randn((16, HEAD_K), generator=gen, device=dev).to(torch.bfloat16)
+        for _ in range(3):
+            for w, s, b in Ws:
+                kernels.qmm_split(x, w, s, b, HEAD_WIDTHS)
+    elif name == "mlp64":
+        mlps = [FusedMLP(*[QuantizedLinear(*make_layer(torch, n, k, 8, torch.bfloat16, gen, dev), bits=8)
+                           for n, k in ((9728, 2560), (9728, 2560), (2560, 9728))]) for _ in range(4)]
+        x = torch.randn((64, 2560), generator=gen, device=dev).to(torch.bfloat16)
+        for _ in range(2):
+            for m in mlps:
+                m(x)
+    elif name == "tc":
+        w, s, b = make_layer(torch, 7168, 4096, 4, torch.bfloat16, gen, dev)
+        x = torch.randn((1024, 4096), generator=gen, device=dev).to(torch.bfloat16)
+        for _ in range(4):
+            kernels.quantized_matmul(x, w, s, b)
+    elif name == "moe16":
+        E, D, I = 64, 2048, 768
+
+        def stack(N, Kd):
+            ws_ = [make_layer(torch, N, Kd, 4, torch.bfloat16, gen, dev) for _ in range(E)]
+            return tuple(torch.stack([w[i] for w in ws_]).contiguous() for i in range(3))
+
+        layer = moe.MoELayer((torch.randn((E, D), generator=gen, device=dev) * 0.02).to(torch.float16),
+                             stack(I, D), stack(I, D), stack(D, I), top_k=4)
+        x = torch.randn((16, D), generator=gen, device=dev).to(torch.bfloat16)
+        for _ in range(3):
+            layer(x)
+    else:
+        raise SystemExit(f"unknown case {name}; known: {sorted(CASES)}")
+    torch.cuda.synchronize()
+    st = kernels.device_status()
+    print(json.dumps({"case": name, "status": st}))
+    return 0 if st == 0 else 1
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -536,7 +607,10 @@ def main():
     ap.add_argument("--impl", default="lq", choices=["lq", "reference"])
     ap.add_argument("--quick", action="store_true", help="headline only (skip the other configs)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--case", default=None, help="run one small profiling case (see CASES) and exit")
     args = ap.parse_args()
+    if args.case:
+        return run_case(args.case)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
