@@ -1,7 +1,7 @@
-"""Benchmark of the MLX affine quantized-matmul path on B200 (BASELINE.json metric:
-"4-bit qmm HBM GB/s at M=1-16 & TFLOP/s at M=2048; MoE tok/s vs MLX CPU").
+"""Benchmark of the MLX affine quantized-matmul path on B200. Metric:
+"4-bit qmm HBM GB/s at M=1-16 & TFLOP/s at M=2048; MoE tok/s vs MLX CPU".
 
-Headline workload (BASELINE config 2, the configuration the metric is quoted on): the fused QKV decode
+Headline workload (the configuration the metric is quoted on): the fused QKV decode
 projection, x bf16 [16, 2560] times a 4-bit g64 [6144, 2560] matrix, output split into q/k/v. One
 step = that projection over a stack of L = 36 distinct layers (36 x 8.85 MB = 318 MB of weights: the
 weights never sit in the 126 MB L2 between uses), captured in one CUDA graph. value = algorithmic bytes
@@ -10,7 +10,8 @@ weights never sit in the 126 MB L2 between uses), captured in one CUDA graph. va
 e2e: the same step through the public API with host buffers: pinned x copied in, the captured layers,
 the last layer's q/k/v copied out, all inside the timed region.
 
-Extra keys report BASELINE configs 1, 3, 4, 5 measured the same way (CUDA events, warm-up, inputs larger
+Extra keys report the other workloads (cfg1: fp16 4096x4096 qmm at M=8; cfg3: 8-bit MLP 2560->9728->2560;
+cfg4: 64-expert top-4 MoE; cfg5: 2048x4096 . 14336x4096 prefill GEMM) measured the same way (CUDA events, warm-up, inputs larger
 than L2 or rotated weight copies), and the CPU baseline (the C/OpenMP restatement of the reference's
 arithmetic, all host cores, a bounded sample).
 
@@ -161,7 +162,7 @@ def run_reference(args):
     gbs, threads, sample = cpu_qkv_sample(seconds=max(2.0, 3.0 * args.steps / 10))
     line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "bf16 (4-bit codes)",
-            "data": "synthetic", "config": {"workload": "fused QKV decode projection, BASELINE config 2, M=16",
+            "data": "synthetic", "config": {"workload": "fused QKV decode projection (cfg2), M=16",
                                             "x": [HEAD_M, HEAD_K], "w": [HEAD_N, HEAD_K], "bits": 4, "group": 64},
             "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                              "sample": sample},
@@ -383,7 +384,7 @@ def _timed_max(torch, fn, steps, warmup, stream, dist):
 
 
 def bench_sharded(torch, dist, ws, steps, warmup, dev, stream):
-    """Configs 3, 4, 5 split over the ranks as BASELINE describes (column shards + all-gather, experts +
+    """cfg3, cfg4, cfg5 split over the ranks (column shards + all-gather, experts +
     all-to-all), each step captured in a CUDA graph with its NCCL collectives; returns rank-0 results."""
     from locals_b200 import moe
     from locals_b200.kernels import QuantizedLinear
@@ -511,7 +512,7 @@ def run_gpu(args):
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (4-bit codes)", "data": "synthetic",
-            "config": {"workload": "fused QKV decode projection (BASELINE config 2), M=16, x bf16 [16,2560], "
+            "config": {"workload": "fused QKV decode projection (cfg2), M=16, x bf16 [16,2560], "
                                    "W 4-bit g64 [6144,2560] -> q[16,32,128] k,v[16,8,128]",
                        "layers_per_step": head_layers, "weights_per_step_MB": round(head["bytes_per_step"] / 1e6, 1),
                        "l2": "inputs larger than L2 (distinct weights per layer, 318 MB per step)",

@@ -88,6 +88,12 @@ int lq_router_logits(const void* x, int x_dtype, const void* w, int w_dtype, flo
  * (T, k) float32. E <= 1024, k <= 32. */
 int lq_route_topk(const float* logits, int T, int E, int k, int mode, uint32_t* inds, float* weights, void* stream);
 
+/* Router logits and top-k in one kernel, one CTA per token (lq_router_logits then lq_route_topk without
+ * the logits round trip): inds (T, k) uint32, weights (T, k) float32; logits (T, E) float32 is written
+ * too when not NULL. E <= 1024, k <= 32. */
+int lq_moe_route(const void* x, int x_dtype, const void* w, int w_dtype, int T, int E, int D, int k, int mode,
+                 uint32_t* inds, float* weights, float* logits, void* stream);
+
 /* Counting sort of P expert ids (locals/moe_kernel.py:28-66,191-197): order (P) = pair ids grouped
  * by ascending expert (ascending pair id within an expert), starts (min(E,P)+1), experts (min(E,P)),
  * nseg (1) and, if pos != NULL, pos (P) = the inverse of order. All int32 device arrays. E <= 8192. */
@@ -106,11 +112,13 @@ int lq_moe_gather(const void* x, const int32_t* order, int P, int k, int D, void
  * glu == 0: out (P, N) = xs . w0_e^T.
  * max_rows bounds the rows of one segment (the token count of the step: a token names an expert at
  * most once). out in dtype, rows in pair order. Rows grouped under expert id E (group with E + 1
- * buckets) are padding: they are skipped and their output rows left unwritten. */
+ * buckets) are padding: they are skipped and their output rows left unwritten.
+ * gather_order != NULL: xs is the token matrix (T, K) and segment row j reads token gather_order[j] /
+ * gather_k (the order of lq_moe_group), fetched inside the kernel -- no lq_moe_gather pass. */
 int lq_moe_experts(const void* xs, const int32_t* starts, const int32_t* experts, const int32_t* nseg, int P,
                    int max_rows, int glu, const uint32_t* w0, const void* s0, const void* b0, const uint32_t* w1,
                    const void* s1, const void* b1, void* out, int E, int N, int K, int bits, int group_size, int dtype,
-                   void* stream);
+                   const int32_t* gather_order, int gather_k, void* stream);
 
 /* y (T, D) = sum over slots r of weights[t, r] * ys[pos[t*k + r], :] in float32, slots in order, rounded
  * to dtype (locals/moe.py:339-348). pos == NULL reads row t*k + r. */

@@ -34,7 +34,8 @@ SIGNATURES = {
     "lq_moe_group": ([_vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp], _i),
     "lq_moe_gather": ([_vp, _vp, _i, _i, _i, _vp, _vp], _i),
     "lq_moe_experts": ([_vp, _vp, _vp, _vp, _i, _i, _i, _u32p, _vp, _vp, _u32p, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i,
-                        _vp], _i),
+                        _vp, _i, _vp], _i),
+    "lq_moe_route": ([_vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp], _i),
     "lq_moe_combine": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp], _i),
     "lq_device_status": ([_i], ctypes.c_uint),
     "lq_last_cuda_error": ([], ctypes.c_char_p),

@@ -25,6 +25,8 @@ int group_run(const uint32_t* inds, int P, int E, int32_t* order, int32_t* start
 int gather_rows_run(const void* x, const int32_t* order, int P, int k, int D, void* xs, cudaStream_t st);
 int combine_run(const void* ys, const float* w, const int32_t* pos, void* y, int T, int k, int D, int dt,
                 cudaStream_t st);
+int router_topk_run(const void* x, int x_dt, const void* w, int w_dt, int T, int E, int D, int k, int mode,
+                    uint32_t* inds, float* weights, float* logits, cudaStream_t st);
 int tc_run(const void* x, const uint32_t* w, const void* s, const void* b, void* y, int M, int N, int K, int bits,
            int dtype, const int* p, cudaStream_t st);
 bool tc_shape_ok(int M, int N, int K, int bits);
@@ -202,6 +204,19 @@ int lq_route_topk(const float* logits, int T, int E, int k, int mode, uint32_t* 
     return finish(route_topk_run(logits, T, E, k, mode, inds, weights, reinterpret_cast<cudaStream_t>(stream)));
 }
 
+int lq_moe_route(const void* x, int x_dtype, const void* w, int w_dtype, int T, int E, int D, int k, int mode,
+                 uint32_t* inds, float* weights, float* logits, void* stream) {
+    if (!x || !w || !inds || !weights) return LQ_E_ARG;
+    if (!is16(x_dtype) || !is16(w_dtype)) return LQ_E_UNSUPPORTED;
+    if (mode != 0 && mode != 1) return LQ_E_ARG;
+    if (T < 1 || E < 1 || E > 1024 || k < 1 || k > 32 || k > E || D < 8 || D % 8) return LQ_E_SHAPE;
+    if (!aligned(x, 16) || !aligned(w, 16)) return LQ_E_ALIGN;
+    int rc = check_device();
+    if (rc) return rc;
+    return finish(router_topk_run(x, x_dtype, w, w_dtype, T, E, D, k, mode, inds, weights, logits,
+                                  reinterpret_cast<cudaStream_t>(stream)));
+}
+
 int lq_moe_group(const uint32_t* inds, int P, int E, int32_t* order, int32_t* starts, int32_t* experts, int32_t* nseg,
                  int32_t* pos, void* stream) {
     if (!inds || !order || !starts || !experts || !nseg) return LQ_E_ARG;
@@ -223,7 +238,7 @@ int lq_moe_gather(const void* x, const int32_t* order, int P, int k, int D, void
 int lq_moe_experts(const void* xs, const int32_t* starts, const int32_t* experts, const int32_t* nseg, int P,
                    int max_rows, int glu, const uint32_t* w0, const void* s0, const void* b0, const uint32_t* w1,
                    const void* s1, const void* b1, void* out, int E, int N, int K, int bits, int group_size, int dtype,
-                   void* stream) {
+                   const int32_t* gather_order, int gather_k, void* stream) {
     int rc = check_common(xs, w0, s0, b0, P, N, K, bits, group_size, dtype);
     if (rc) return rc;
     if (!starts || !experts || !nseg || !out) return LQ_E_ARG;
@@ -253,8 +268,11 @@ int lq_moe_experts(const void* xs, const int32_t* starts, const int32_t* experts
     m.s[1] = glu ? s1 : s0;
     m.b[1] = glu ? b1 : b0;
     m.rows_total[0] = m.rows_total[1] = E * N;
+    if (gather_order && gather_k < 1) return LQ_E_ARG;
+    a.gather = gather_order;
+    a.gather_k = gather_k;
     const int nseg_grid = (E + 1) < P ? (E + 1) : P;  // (one more for a padding bucket, expert id E)
-    return finish(qmv_run(xs, P, m, glu ? 2 : 1, a, bits, dtype, nullptr, max_rows, nseg_grid,
+    return finish(qmv_run(xs, gather_order ? 1 : P, m, glu ? 2 : 1, a, bits, dtype, nullptr, max_rows, nseg_grid,
                           reinterpret_cast<cudaStream_t>(stream)));
 }
 

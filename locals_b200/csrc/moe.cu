@@ -17,9 +17,27 @@
 #include <stdint.h>
 
 #include "lq_host.h"
+#include "lq_ptx.cuh"
 #include "lq_status.cuh"
 
 namespace lq {
+
+// Launch with programmatic dependent launch: the kernel may start while the previous kernel on the stream
+// finishes; it calls grid_dep_wait() before reading anything that kernel wrote.
+template <typename... KArgs, typename... Args>
+static int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...));
+}
 
 __device__ __forceinline__ void unpack8(uint4 u, int dt, float* f) {
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
@@ -40,6 +58,8 @@ __device__ __forceinline__ void unpack8(uint4 u, int dt, float* f) {
 // grid: T * ceil(E / 4) blocks of 128 threads (4 warps = 4 experts of one token)
 __global__ void router_logits_kernel(const void* x, int x_dt, const void* w, int w_dt, float* logits, int T, int E,
                                      int D) {
+    grid_dep_wait();
+    grid_dep_launch();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int eb = (E + 3) / 4;
     const int t = blockIdx.x / eb;
@@ -62,9 +82,52 @@ __global__ void router_logits_kernel(const void* x, int x_dt, const void* w, int
 
 constexpr int TOPK_MAX_PER_LANE = 32;  // E <= 1024
 
+// k rounds of a warp argmax over E scores held `per` per lane (expert lane + 32 j), ties to the lower
+// index, then renormalisation; lane 0 writes k indices and weights. NaN scores rank below every number.
+__device__ __forceinline__ void topk_select(float* sc, int per, int E, int k, int lane, uint32_t* inds,
+                                            float* weights) {
+    for (int j = 0; j < per; ++j)
+        if (isnan(sc[j])) sc[j] = -2.0f;
+    float picked_sum = 0.0f;
+    float picked[32];
+    uint32_t which[32];
+    for (int r = 0; r < k; ++r) {
+        float best = -3.0f;
+        int best_e = E;
+        for (int j = 0; j < per; ++j) {
+            const int e = lane + 32 * j;
+            if (e < E && sc[j] > best) {  // strict: the lower index of this lane wins ties
+                best = sc[j];
+                best_e = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oe = __shfl_xor_sync(0xffffffffu, best_e, o);
+            if (ob > best || (ob == best && oe < best_e)) {
+                best = ob;
+                best_e = oe;
+            }
+        }
+        if (best_e < E && (best_e & 31) == lane) sc[best_e >> 5] = -3.0f;
+        picked[r] = best < -1.5f ? 0.0f : best;
+        which[r] = uint32_t(best_e < E ? best_e : E - 1);
+        picked_sum += picked[r];
+    }
+    if (lane == 0) {
+        for (int r = 0; r < k; ++r) {
+            inds[r] = which[r];
+            weights[r] = picked[r] / picked_sum;
+        }
+    }
+}
+
 // one warp per token; 4 tokens per block
 __global__ void route_topk_kernel(const float* logits, int T, int E, int k, int mode, uint32_t* inds,
                                   float* weights) {
+    grid_dep_wait();
+    grid_dep_launch();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * 4 + warp;
     if (t >= T) return;
@@ -99,47 +162,14 @@ __global__ void route_topk_kernel(const float* logits, int T, int E, int k, int 
             sc[j] = e < E ? (isnan(v) ? 0.0f : v) : -1.0f;
         }
     }
-    // NaN scores (softmax of NaN logits) rank below every number; the result still names k distinct experts
-    for (int j = 0; j < per; ++j)
-        if (isnan(sc[j])) sc[j] = -2.0f;
-    float picked_sum = 0.0f;
-    float picked[32];
-    uint32_t which[32];
-    for (int r = 0; r < k; ++r) {
-        float best = -3.0f;
-        int best_e = E;
-        for (int j = 0; j < per; ++j) {
-            const int e = lane + 32 * j;
-            if (e < E && sc[j] > best) {  // strict: the lower index of this lane wins ties
-                best = sc[j];
-                best_e = e;
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-            const int oe = __shfl_xor_sync(0xffffffffu, best_e, o);
-            if (ob > best || (ob == best && oe < best_e)) {
-                best = ob;
-                best_e = oe;
-            }
-        }
-        if (best_e < E && (best_e & 31) == lane) sc[best_e >> 5] = -3.0f;
-        picked[r] = best < -1.5f ? 0.0f : best;
-        which[r] = uint32_t(best_e < E ? best_e : E - 1);
-        picked_sum += picked[r];
-    }
-    if (lane == 0) {
-        for (int r = 0; r < k; ++r) {
-            inds[size_t(t) * k + r] = which[r];
-            weights[size_t(t) * k + r] = picked[r] / picked_sum;
-        }
-    }
+    topk_select(sc, per, E, k, lane, inds + size_t(t) * k, weights + size_t(t) * k);
 }
 
 // One CTA of 1024 threads. order/starts/experts/nseg as lq_moe_group; pos = inverse of order (optional).
 __global__ void group_kernel(const uint32_t* inds, int P, int E, int32_t* order, int32_t* starts, int32_t* experts,
                              int32_t* nseg, int32_t* pos) {
+    grid_dep_wait();
+    grid_dep_launch();
     extern __shared__ int32_t sh[];
     int32_t* cnt = sh;       // E
     int32_t* base = sh + E;  // E
@@ -182,6 +212,8 @@ __global__ void group_kernel(const uint32_t* inds, int P, int E, int32_t* order,
 
 // xs[j] = x[order[j] / k]: one warp per row, 16-byte copies
 __global__ void gather_rows_kernel(const uint16_t* x, const int32_t* order, int P, int k, int D, uint16_t* xs) {
+    grid_dep_wait();
+    grid_dep_launch();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= P) return;
     const int tok = order[warp] / k;
@@ -193,6 +225,8 @@ __global__ void gather_rows_kernel(const uint16_t* x, const int32_t* order, int 
 // y[t, d] = sum_r w[t, r] * ys[row(t, r), d]; row = pos[t*k + r] if pos, else t*k + r
 __global__ void combine_kernel(const uint16_t* ys, const float* w, const int32_t* pos, uint16_t* y, int T, int k, int D,
                                int dt) {
+    grid_dep_wait();
+    grid_dep_launch();
     const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= size_t(T) * D) return;
     const int t = int(i / D), d = int(i % D);
@@ -218,40 +252,111 @@ __global__ void combine_kernel(const uint16_t* ys, const float* w, const int32_t
     }
 }
 
+// Router logits and top-k of one token per CTA (256 threads): warps compute the E float32 dot products
+// (16-byte loads of x and of each expert's router row), the logits stay in shared memory, and warp 0
+// picks the top k exactly as route_topk_kernel does. logits_out may be null.
+constexpr int ROUTE_MAX_E = 1024;
+__global__ void __launch_bounds__(256) router_topk_kernel(const void* x, int x_dt, const void* w, int w_dt, int T,
+                                                          int E, int D, int k, int mode, uint32_t* inds, float* weights,
+                                                          float* logits_out) {
+    grid_dep_wait();
+    grid_dep_launch();
+    __shared__ float lg[ROUTE_MAX_E];
+    const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (t >= T) return;
+    const uint4* xr = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + size_t(t) * D);
+    for (int e = warp; e < E; e += 8) {
+        const uint4* wr = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(w) + size_t(e) * D);
+        float acc = 0.0f;
+        for (int i = lane; i < D / 8; i += 32) {
+            float xf[8], wf[8];
+            unpack8(xr[i], x_dt, xf);
+            unpack8(wr[i], w_dt, wf);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc = fmaf(xf[j], wf[j], acc);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) {
+            lg[e] = acc;
+            if (logits_out) logits_out[size_t(t) * E + e] = acc;
+        }
+    }
+    __syncthreads();
+    if (warp != 0) return;
+    const int per = (E + 31) / 32;
+    float sc[TOPK_MAX_PER_LANE];
+    if (mode == 0) {
+        float mx = -INFINITY;
+        for (int j = 0; j < per; ++j) {
+            const int e = lane + 32 * j;
+            sc[j] = e < E ? lg[e] : -INFINITY;
+            mx = fmaxf(mx, sc[j]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float tot = 0.0f;
+        for (int j = 0; j < per; ++j) {
+            const int e = lane + 32 * j;
+            sc[j] = e < E ? expf(sc[j] - mx) : 0.0f;
+            tot += sc[j];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+        for (int j = 0; j < per; ++j) {
+            const int e = lane + 32 * j;
+            sc[j] = e < E ? sc[j] / tot : -1.0f;
+        }
+    } else {
+        for (int j = 0; j < per; ++j) {
+            const int e = lane + 32 * j;
+            const float v = e < E ? 1.0f / (1.0f + expf(-lg[e])) : -1.0f;
+            sc[j] = e < E ? (isnan(v) ? 0.0f : v) : -1.0f;
+        }
+    }
+    topk_select(sc, per, E, k, lane, inds + size_t(t) * k, weights + size_t(t) * k);
+}
+
+int router_topk_run(const void* x, int x_dt, const void* w, int w_dt, int T, int E, int D, int k, int mode,
+                    uint32_t* inds, float* weights, float* logits, cudaStream_t st) {
+    return launch_pdl(router_topk_kernel, dim3(T), dim3(256), 0, st, x, x_dt, w, w_dt, T, E, D, k, mode, inds, weights,
+                      logits);
+}
+
 int router_logits_run(const void* x, int x_dt, const void* w, int w_dt, float* logits, int T, int E, int D,
                       cudaStream_t st) {
     const int blocks = T * ((E + 3) / 4);
-    router_logits_kernel<<<blocks, 128, 0, st>>>(x, x_dt, w, w_dt, logits, T, E, D);
-    return cuda_status(cudaGetLastError());
+    return launch_pdl(router_logits_kernel, dim3(blocks), dim3(128), 0, st, x, x_dt, w, w_dt, logits, T, E, D);
 }
 
 int route_topk_run(const float* logits, int T, int E, int k, int mode, uint32_t* inds, float* weights,
                    cudaStream_t st) {
-    route_topk_kernel<<<(T + 3) / 4, 128, 0, st>>>(logits, T, E, k, mode, inds, weights);
-    return cuda_status(cudaGetLastError());
+    return launch_pdl(route_topk_kernel, dim3((T + 3) / 4), dim3(128), 0, st, logits, T, E, k, mode, inds, weights);
 }
 
 int group_run(const uint32_t* inds, int P, int E, int32_t* order, int32_t* starts, int32_t* experts, int32_t* nseg,
               int32_t* pos, cudaStream_t st) {
-    group_kernel<<<1, 1024, size_t(2) * E * sizeof(int32_t), st>>>(inds, P, E, order, starts, experts, nseg, pos);
-    return cuda_status(cudaGetLastError());
+    const size_t smem = size_t(2) * E * sizeof(int32_t);
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return LQ_E_CUDA;
+    }
+    return launch_pdl(group_kernel, dim3(1), dim3(1024), smem, st, inds, P, E, order, starts, experts, nseg, pos);
 }
 
 int gather_rows_run(const void* x, const int32_t* order, int P, int k, int D, void* xs, cudaStream_t st) {
     const int threads = 256;
     const int blocks = (P * 32 + threads - 1) / threads;
-    gather_rows_kernel<<<blocks, threads, 0, st>>>(reinterpret_cast<const uint16_t*>(x), order, P, k, D,
-                                                   reinterpret_cast<uint16_t*>(xs));
-    return cuda_status(cudaGetLastError());
+    return launch_pdl(gather_rows_kernel, dim3(blocks), dim3(threads), 0, st, reinterpret_cast<const uint16_t*>(x),
+                      order, P, k, D, reinterpret_cast<uint16_t*>(xs));
 }
 
 int combine_run(const void* ys, const float* w, const int32_t* pos, void* y, int T, int k, int D, int dt,
                 cudaStream_t st) {
     const size_t n = size_t(T) * D;
     const int threads = 256;
-    combine_kernel<<<unsigned((n + threads - 1) / threads), threads, 0, st>>>(
-        reinterpret_cast<const uint16_t*>(ys), w, pos, reinterpret_cast<uint16_t*>(y), T, k, D, dt);
-    return cuda_status(cudaGetLastError());
+    return launch_pdl(combine_kernel, dim3(unsigned((n + threads - 1) / threads)), dim3(threads), 0, st,
+                      reinterpret_cast<const uint16_t*>(ys), w, pos, reinterpret_cast<uint16_t*>(y), T, k, D, dt);
 }
 
 }  // namespace lq

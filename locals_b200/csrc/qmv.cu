@@ -301,11 +301,13 @@ __global__ void __launch_bounds__(QMV_THREADS, (MT * NMAT <= 2) ? 2 : 1)
         const int kg = a.K / 64;  // groups per row
         const int vb = a.sb_vec;  // bytes per cp.async
         const int units_row = S::SBROW / vb;
+        const bool gather = a.gather != nullptr;
+        // weights (TMA, lane 0) and scales/biases (cp.async, all lanes) of local chunk i into stage s
         auto load_weights = [&](int i, int s) {
             const uint32_t st = smem_base + s * S::STAGE_BYTES;
             const int c = c_begin + (i % nloc);
             if (lane == 0) {
-                mbar_arrive_expect_tx(&full[s], S::TMA_BYTES);
+                mbar_arrive_expect_tx(&full[s], gather ? NMAT * S::W_BYTES : S::TMA_BYTES);
 #pragma unroll
                 for (int m = 0; m < NMAT; ++m)
                     tma_load_3d(smem + s * S::STAGE_BYTES + m * S::W_BYTES, tw[m], &full[s], 0,
@@ -337,19 +339,46 @@ __global__ void __launch_bounds__(QMV_THREADS, (MT * NMAT <= 2) ? 2 : 1)
                     }
                 }
             }
-            cp_async_arrive(&full[s]);
         };
+        // x slice of local chunk i: one TMA box, or (gather) 16-byte cp.async per token row and chunk,
+        // written in the same swizzled layout, zero-filled past the segment and past K
         auto load_x = [&](int i, int s) {
-            if (lane == 0) {
-                const int tb = i / nloc, c = c_begin + (i % nloc);
-                tma_load_3d(smem + s * S::STAGE_BYTES + NMAT * S::W_BYTES, &tm_x, &full[s], 0,
-                            seg_row0 + tb * S::MTOK, c * (S::BK / 64), pol_x);
+            const int tb = i / nloc, c = c_begin + (i % nloc);
+            if (!gather) {
+                if (lane == 0)
+                    tma_load_3d(smem + s * S::STAGE_BYTES + NMAT * S::W_BYTES, &tm_x, &full[s], 0,
+                                seg_row0 + tb * S::MTOK, c * (S::BK / 64), pol_x);
+                return;
+            }
+            const uint32_t xdst = smem_base + s * S::STAGE_BYTES + NMAT * S::W_BYTES;
+            constexpr int CPR = S::BK / 8;  // 16-byte chunks per token row
+            const uint8_t* xb = reinterpret_cast<const uint8_t*>(a.x);
+            for (int ci = lane; ci < S::MTOK * CPR; ci += 32) {
+                const int tok = ci / CPR, cc = ci % CPR;
+                const int seg = cc >> 3, ch = cc & 7;
+                const int r = tb * S::MTOK + tok;
+                const int kidx = c * S::BK + cc * 8;
+                const bool valid = r < seg_rows && kidx < a.K;
+                size_t off = 0;
+                if (valid) off = (size_t(a.gather[seg_row0 + r] / a.gather_k) * a.K + kidx) * 2;
+                cp_async(xdst + seg * (S::MTOK * 128) + tok * 128 + ((ch ^ (tok & 7)) << 4), xb + off, 16, valid);
             }
         };
         const int pre = total < ns ? total : ns;
-        for (int i = 0; i < pre; ++i) load_weights(i, i);
-        if (!a.grouped) grid_dep_wait();  // x may be the previous kernel's output
-        for (int i = 0; i < pre; ++i) load_x(i, i);
+        if (!a.grouped) {
+            for (int i = 0; i < pre; ++i) {
+                load_weights(i, i);
+                cp_async_arrive(&full[i]);
+            }
+            grid_dep_wait();  // x may be the previous kernel's output
+            for (int i = 0; i < pre; ++i) load_x(i, i);
+        } else {  // (the grid dependency was resolved at entry: starts / experts come from the grouping)
+            for (int i = 0; i < pre; ++i) {
+                load_weights(i, i);
+                load_x(i, i);
+                cp_async_arrive(&full[i]);
+            }
+        }
         if (lane == 0) grid_dep_launch();
         for (int i = pre; i < total && ok; ++i) {
             const int s = i % ns;
@@ -357,6 +386,7 @@ __global__ void __launch_bounds__(QMV_THREADS, (MT * NMAT <= 2) ? 2 : 1)
             if (!ok) break;
             load_weights(i, s);
             load_x(i, s);
+            cp_async_arrive(&full[s]);
         }
         __syncwarp();
     } else {
@@ -539,6 +569,7 @@ static int qmv_launch_t(const void* x, int x_rows, const QmvMats& mats, QmvArgs 
     }
     const int kg = K / 64;
     a.sb_vec = (S::SBROW == 16 && kg % 8 == 0) ? 16 : (kg % 4 == 0) ? 8 : 4;
+    a.x = x;
 
     auto kern = qmv_kernel<T, BITS, MT, WK, NMAT>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));

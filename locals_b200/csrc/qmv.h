@@ -25,6 +25,9 @@ struct QmvArgs {
     const int32_t* experts;
     const int32_t* nseg;
     int n_experts;
+    const void* x;          // x base (gather mode reads rows through it)
+    const int32_t* gather;  // grouped mode: segment row j reads x row gather[j] / gather_k (null: row j)
+    int gather_k;
 };
 
 struct QmvMats {

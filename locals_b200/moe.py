@@ -73,11 +73,13 @@ def gather(x: torch.Tensor, order: torch.Tensor, k: int) -> torch.Tensor:
 
 
 def experts(xs: torch.Tensor, grouping, mats: Sequence, N: int, max_rows: int, bits: int = 4,
-            group_size: int = 64) -> torch.Tensor:
-    """Grouped projections over pair-ordered rows xs (P, K): mats = [gate, up] (SwiGLU) or [w];
-    each (weight (E, N, K*bits/32), scales (E, N, K/64), biases)."""
+            group_size: int = 64, gather_k: int = 0) -> torch.Tensor:
+    """Grouped projections: mats = [gate, up] (SwiGLU) or [w]; each (weight (E, N, K*bits/32), scales
+    (E, N, K/64), biases). With gather_k, xs is the token matrix (T, K) and the kernel fetches each pair's
+    token (grouping order // gather_k) itself; otherwise xs holds one row per pair in expert order."""
     order, starts, experts_, nseg, _ = grouping
-    P, K = xs.shape
+    K = xs.shape[-1]
+    P = order.numel()
     E = mats[0][0].shape[0]
     glu = len(mats) == 2
     w0, s0, b0 = mats[0]
@@ -85,7 +87,8 @@ def experts(xs: torch.Tensor, grouping, mats: Sequence, N: int, max_rows: int, b
     out = torch.empty((P, N), dtype=xs.dtype, device=xs.device)
     call("lq_moe_experts", xs.data_ptr(), starts.data_ptr(), experts_.data_ptr(), nseg.data_ptr(), P, max_rows,
          1 if glu else 0, w0.data_ptr(), s0.data_ptr(), b0.data_ptr(), w1.data_ptr(), s1.data_ptr(), b1.data_ptr(),
-         out.data_ptr(), E, N, K, bits, group_size, dtype_code(xs.dtype), _stream())
+         out.data_ptr(), E, N, K, bits, group_size, dtype_code(xs.dtype),
+         order.data_ptr() if gather_k else None, gather_k, _stream())
     return out
 
 
@@ -98,6 +101,22 @@ def combine(ys: torch.Tensor, weights: torch.Tensor, pos: Optional[torch.Tensor]
     return y
 
 
+GATHER_IN_KERNEL_MAX_ROWS = 16  # up to this many tokens the GLU kernel fetches the pairs' tokens itself
+
+
+def route(x: torch.Tensor, w: torch.Tensor, k: int, mode: int = SOFTMAX):
+    """Router logits and top-k in one kernel: (inds int32 (T, k), weights float32 (T, k))."""
+    D = x.shape[-1]
+    x2 = x.reshape(-1, D).contiguous()
+    _check_cuda(x2, w)
+    T, E = x2.shape[0], w.shape[0]
+    inds = torch.empty((T, k), dtype=torch.int32, device=x.device)
+    wts = torch.empty((T, k), dtype=torch.float32, device=x.device)
+    call("lq_moe_route", x2.data_ptr(), dtype_code(x.dtype), w.data_ptr(), dtype_code(w.dtype), T, E, D, k, mode,
+         inds.data_ptr(), wts.data_ptr(), None, _stream())
+    return inds, wts
+
+
 def switch_glu(x: torch.Tensor, inds: torch.Tensor, gate, up, down, bits: int = 4, group_size: int = 64,
                grouping=None) -> torch.Tensor:
     """mlx-lm SwitchGLU for rows x (M, D) and experts inds (M, k): (M*k, D) rows in pair order, with the
@@ -108,13 +127,17 @@ def switch_glu(x: torch.Tensor, inds: torch.Tensor, gate, up, down, bits: int = 
     D = x.shape[-1]
     if grouping is None:
         grouping = group(inds, E)
-    xs = gather(x, grouping[0], k)
-    h = experts(xs, grouping, [gate, up], I, max_rows=M, bits=bits, group_size=group_size)
+    if M <= GATHER_IN_KERNEL_MAX_ROWS:
+        h = experts(x.contiguous(), grouping, [gate, up], I, max_rows=M, bits=bits, group_size=group_size,
+                    gather_k=k)
+    else:
+        xs = gather(x, grouping[0], k)
+        h = experts(xs, grouping, [gate, up], I, max_rows=M, bits=bits, group_size=group_size)
     return experts(h, grouping, [down], D, max_rows=M, bits=bits, group_size=group_size)
 
 
 class MoELayer:
-    """Router + top-k experts + combine over stacked MLX-affine experts."""
+    """Router + top-k experts + combine over stacked MLX-affine experts (softmax routing, top-k renormalised)."""
 
     def __init__(self, router_w: torch.Tensor, gate, up, down, top_k: int, mode: int = SOFTMAX, bits: int = 4,
                  group_size: int = 64):
@@ -123,7 +146,7 @@ class MoELayer:
         self.n_experts = gate[0].shape[0]
 
     def route(self, x: torch.Tensor):
-        return route_topk(router_logits(x, self.router_w), self.top_k, self.mode)
+        return route(x, self.router_w, self.top_k, self.mode)
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         D = x.shape[-1]

@@ -1,7 +1,6 @@
 """Multi-GPU sharding of the quantized-matmul path (one process per GPU, torch.distributed over NCCL).
 
-The reference runs one model on one Apple GPU (no distributed code, SURVEY: "collective call sites: none");
-the partitioning here is the one BASELINE's north star asks for:
+The reference runs one model on one Apple GPU and has no distributed code; the partitioning here:
 
 * ``ColumnShardedLinear`` -- a quantized linear split by output rows (columns of y): rank r keeps rows
   [r N/G, (r+1) N/G) of the packed weights, scales and biases (quantization groups run along K, so each

@@ -28,7 +28,7 @@
  *                     locals/qmv_multi.py:57-75 and locals/qmv_frag.py:356-359.
  *   lqo_router        float32 x @ W^T of 16-bit x and W (locals/moe.py:86-89,134-139).
  *   lqo_topk_softmax  softmax over experts in float32, the k largest (ties to the
- *                     lower index), renormalised to sum 1 (
+ *                     lower index), renormalised to sum 1 (the routing of a softmax MoE block;
  *                     tie rule of locals/moe.py:32-35,51-61, renormalisation of
  *                     locals/moe.py:63-70).
  *   lqo_topk_sigmoid  locals/moe.py:36-82 (sigmoid scores, NaN -> 0, ties to the

@@ -82,8 +82,8 @@ def from_bits(u, dtype) -> np.ndarray:
 
 def quantize(w, group_size: int = 64, bits: int = 4, dtype="float32"):
     """MLX affine quantization of ``w`` (N, K) -> (packed uint32 (N, K*bits/32), scales, biases), the
-    scales and biases rounded to ``dtype`` after the codes are chosen (float32 input, as BASELINE's
-    fp32 weights)."""
+    scales and biases rounded to ``dtype`` after the codes are chosen (float32 input: the
+    weights are generated in fp32)."""
     w = _f32(w)
     N, K = w.shape
     assert K % group_size == 0 and group_size % (32 // bits) == 0

@@ -9,7 +9,7 @@ kernels are both checked against the reference's own arithmetic:
 * dequant: `scale * q + bias` (locals/kernels.py:64,77);
 * qmm: per group `s * sum(q * x) + b * sum(x)` accumulated in float32 (locals/qmv_multi.py:57-75);
 * routing: sigmoid, k rounds of argmax with ties to the lower index, renormalisation
-  (locals/moe.py:36-82); softmax variant of BASELINE config 4;
+  (locals/moe.py:36-82); softmax variant of a softmax-routed MoE block;
 * grouping: the counting sort of locals/moe_kernel.py:28-66 (stable within an expert);
 * quantize: MLX's affine algorithm (mx.quantize; the reference calls it in
   tests/test_kernel_patching.py:163). MLX is not available here, so these vectors pin our

@@ -1,5 +1,5 @@
 """Shared helpers for the parity tests: seeded MLX-format weights made by the CPU oracle, moved to
-the GPU, and the tolerance of BASELINE's north star."""
+the GPU, and the output tolerance (1e-2 of the largest reference value)."""
 
 from __future__ import annotations
 

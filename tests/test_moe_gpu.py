@@ -1,4 +1,4 @@
-"""Parity of the routed-MoE kernels against the CPU oracle on the GPU (BASELINE config 4: 64 experts,
+"""Parity of the routed-MoE kernels against the CPU oracle on the GPU (64 experts,
 top-4, hidden 2048, expert intermediate 768, 4-bit g64, router Wr fp16, x bf16, softmax routing).
 
 Selection parity compares per-token expert sets (tests/test_flint.py:59-66); tokens whose 4th and 5th
@@ -132,3 +132,18 @@ def test_moe_layer(cuda, M):
     ref = O.moe(x, gi.astype(np.uint32), wts.cpu().numpy(), [g + (4,) for g in gate], [u + (4,) for u in up],
                 [d + (4,) for d in down], "bfloat16")
     assert rel_err(y.float().cpu().numpy(), ref) <= TOL_REL
+
+
+@pytest.mark.parametrize("T", [1, 16, 512])
+def test_route_fused(cuda, T):
+    # router logits + top-k in one kernel: same expert sets as the two-kernel path, weights within 1e-5
+    import torch
+    from locals_b200 import moe
+
+    rng = np.random.default_rng(T)
+    x, wr = _router_inputs(rng, T, 64, 2048)
+    xt, wt = x_torch(x, "bfloat16", cuda), torch.from_numpy(wr).to(cuda, torch.float16)
+    i1, w1 = moe.route(xt, wt, 4)
+    i2, w2 = moe.route_topk(moe.router_logits(xt, wt), 4)
+    assert np.array_equal(i1.cpu().numpy(), i2.cpu().numpy())
+    np.testing.assert_allclose(w1.cpu().numpy(), w2.cpu().numpy(), rtol=1e-5, atol=1e-6)

@@ -1,6 +1,6 @@
 """Parity of the decode family (qmv) against the CPU oracle, through the C ABI (ctypes) on the GPU.
 
-Tolerance (BASELINE north star): max|y - ref| <= 1e-2 * max|ref| with fp32 accumulation; the reference's
+Tolerance: max|y - ref| <= 1e-2 * max|ref| with fp32 accumulation; the reference's
 own kernel tests use 0.02 * (1 + max|ref|) (tests/test_q35_kernels.py:60-93). Codes are bit-exact:
 the GPU quantizer must reproduce the oracle's codes, scales and biases exactly.
 """
@@ -29,8 +29,8 @@ def _run(cuda, M, N, K, bits, dtype, seed, choice=None):
     return y.float().cpu().numpy(), ref
 
 
-# BASELINE configs 1-3 at their real sizes (config 1: fp16 M=8; config 2: fused QKV 6144x2560 bf16;
-# config 3: 8-bit MLP projections)
+# the decode workloads at their real sizes (fp16 4096x4096 at M=8; the fused QKV 6144x2560 bf16;
+# the 8-bit MLP projections)
 @pytest.mark.parametrize("M,N,K,bits,dtype", [
     (8, 4096, 4096, 4, "float16"),
     (1, 6144, 2560, 4, "bfloat16"),
@@ -122,7 +122,7 @@ def test_gpu_dequantize(cuda, bits):
 
 
 def test_fused_qkv_split(cuda):
-    """q/k/v concatenated [6144, 2560], output split into q [M,32,128], k/v [M,8,128]."""
+    """The fused QKV decode projection: q/k/v concatenated [6144, 2560], output split into q [M,32,128], k/v [M,8,128]."""
     from locals_b200 import kernels
     from locals_b200.fuse import FusedQKV
     from locals_b200.kernels import QuantizedLinear
@@ -146,7 +146,7 @@ def test_fused_qkv_split(cuda):
 
 @pytest.mark.parametrize("M", [1, 4, 16, 64])
 def test_fused_mlp_8bit(cuda, M):
-    """y = down(silu(gate x) * (up x)), 8-bit, gate/up fused with the SiLU.mul epilogue."""
+    """The 8-bit MLP block: y = down(silu(gate x) * (up x)), 8-bit, gate/up fused with the SiLU.mul epilogue."""
     from locals_b200.fuse import FusedMLP
     from locals_b200.kernels import QuantizedLinear
 

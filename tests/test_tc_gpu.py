@@ -1,6 +1,6 @@
 """Parity of the prefill family (tcgen05 GEMM with fused dequant) against the CPU oracle on the GPU.
 
-x bf16 [2048, 4096], W 4-bit g64 [14336, 4096] -> y [2048, 14336], fp32 accumulation;
+The prefill workload: x bf16 [2048, 4096], W 4-bit g64 [14336, 4096] -> y [2048, 14336], fp32 accumulation;
 tolerance max|y - ref| <= 1e-2 * max|ref|. At the full size the oracle checks a sample of rows (the
 kernel's rows are independent: row m of y depends on row m of x only), plus the whole output against a
 dequantize + fp32 matmul on the GPU's own dequantized weights.
