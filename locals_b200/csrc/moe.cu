@@ -253,10 +253,11 @@ __global__ void combine_kernel(const uint16_t* ys, const float* w, const int32_t
 }
 
 // Router logits and top-k of one token per CTA (256 threads): warps compute the E float32 dot products
-// (16-byte loads of x and of each expert's router row), the logits stay in shared memory, and warp 0
-// picks the top k exactly as route_topk_kernel does. logits_out may be null.
+// (16-byte loads of x and of each expert's router row; 16 warps, each expert's row split over a warp),
+// the logits stay in shared memory, and warp 0 picks the top k exactly as route_topk_kernel does.
+// logits_out may be null.
 constexpr int ROUTE_MAX_E = 1024;
-__global__ void __launch_bounds__(256) router_topk_kernel(const void* x, int x_dt, const void* w, int w_dt, int T,
+__global__ void __launch_bounds__(512) router_topk_kernel(const void* x, int x_dt, const void* w, int w_dt, int T,
                                                           int E, int D, int k, int mode, uint32_t* inds, float* weights,
                                                           float* logits_out) {
     grid_dep_wait();
@@ -265,7 +266,7 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const void* x, int x_d
     const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (t >= T) return;
     const uint4* xr = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + size_t(t) * D);
-    for (int e = warp; e < E; e += 8) {
+    for (int e = warp; e < E; e += 16) {
         const uint4* wr = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(w) + size_t(e) * D);
         float acc = 0.0f;
         for (int i = lane; i < D / 8; i += 32) {
@@ -319,7 +320,7 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const void* x, int x_d
 
 int router_topk_run(const void* x, int x_dt, const void* w, int w_dt, int T, int E, int D, int k, int mode,
                     uint32_t* inds, float* weights, float* logits, cudaStream_t st) {
-    return launch_pdl(router_topk_kernel, dim3(T), dim3(256), 0, st, x, x_dt, w, w_dt, T, E, D, k, mode, inds, weights,
+    return launch_pdl(router_topk_kernel, dim3(T), dim3(512), 0, st, x, x_dt, w, w_dt, T, E, D, k, mode, inds, weights,
                       logits);
 }
 

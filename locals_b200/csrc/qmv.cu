@@ -357,8 +357,9 @@ __global__ void __launch_bounds__(QMV_THREADS, (MT * NMAT <= 2) ? 2 : 1)
                 const int tok = ci / CPR, cc = ci % CPR;
                 const int seg = cc >> 3, ch = cc & 7;
                 const int r = tb * S::MTOK + tok;
+                if (r >= seg_rows) continue;  // (token slots past the segment: their outputs are never stored)
                 const int kidx = c * S::BK + cc * 8;
-                const bool valid = r < seg_rows && kidx < a.K;
+                const bool valid = kidx < a.K;
                 size_t off = 0;
                 if (valid) off = (size_t(a.gather[seg_row0 + r] / a.gather_k) * a.K + kidx) * 2;
                 cp_async(xdst + seg * (S::MTOK * 128) + tok * 128 + ((ch ^ (tok & 7)) << 4), xb + off, 16, valid);
@@ -653,7 +654,17 @@ int qmv_run(const void* x, int x_rows, const QmvMats& mats, int nmat, QmvArgs a,
     int MT = p ? p[0] : 0, WK = p ? p[1] : 0, ks = p ? p[2] : 0, ns = p ? p[3] : 0;
     if (a.M < 1 || max_seg_rows < 1) return LQ_E_SHAPE;
     if (!qmv_shape_ok(a.K, bits)) return LQ_E_SHAPE;
-    if (MT == 0) MT = max_seg_rows <= 8 ? 1 : max_seg_rows <= 16 ? 2 : max_seg_rows <= 32 ? 4 : 8;
+    if (MT == 0) {
+        int rows = max_seg_rows;
+        if (a.grouped) {
+            // rows per used expert, about P / min(E, P) (a token names an expert at most once); longer
+            // segments take extra token blocks, which re-read their expert's weights from L2
+            const int segs = a.n_experts < a.M ? a.n_experts : a.M;
+            const int expect = (a.M + segs - 1) / segs;
+            rows = expect * 2 < max_seg_rows ? expect * 2 : max_seg_rows;
+        }
+        MT = rows <= 8 ? 1 : rows <= 16 ? 2 : rows <= 32 ? 4 : 8;
+    }
     if (MT != 1 && MT != 2 && MT != 4 && MT != 8) return LQ_E_ARG;
     const int nchunk = (a.K + (2048 / bits) - 1) / (2048 / bits);
     const int sms = device_info().sm_count;
