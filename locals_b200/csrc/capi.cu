@@ -30,6 +30,9 @@ int router_topk_run(const void* x, int x_dt, const void* w, int w_dt, int T, int
 int tc_run(const void* x, const uint32_t* w, const void* s, const void* b, void* y, int M, int N, int K, int bits,
            int dtype, const int* p, cudaStream_t st);
 bool tc_shape_ok(int M, int N, int K, int bits);
+bool tcv_shape_ok(int M, int K, int bits);
+int tcv_run(const void* x, int M, const QmvMats& mats, int nmat, int N, int K, int nout, void* const* outs,
+            const int* seg_end, const int* ldo, int bits, int dtype, const int* p, cudaStream_t st);
 }  // namespace lq
 
 using namespace lq;
@@ -52,6 +55,16 @@ static int check_common(const void* x, const uint32_t* w, const void* s, const v
     if (M < 1 || N < 1 || K < 64 || K % 64) return LQ_E_SHAPE;
     if (!aligned(x, 16) || !aligned(w, 16) || !aligned(s, 4) || !aligned(b, 4)) return LQ_E_ALIGN;
     return check_device();
+}
+
+// Decode family for the library's own pick: the tensor-core family (tcv) once the weights of one call
+// are large enough to keep the GPU streaming or the token tile is wide, else the mma.sync family (qmv),
+// whose two CTAs per SM let one call's weights load while the previous call still runs. Measured on
+// B200: qmv wins the 8 MB fused QKV projection up to 32 tokens; tcv wins the 25-50 MB 8-bit MLP
+// projections from 16 tokens and everything from 33 tokens.
+static bool prefer_tcv(int M, double weight_bytes, int K, int bits) {
+    if (!tcv_shape_ok(M, K, bits)) return false;
+    return M > 32 || (M > 8 && weight_bytes >= 24.0e6);
 }
 
 static QmvMats one_matrix(const uint32_t* w, const void* s, const void* b, int rows) {
@@ -90,8 +103,16 @@ static int qmm_common(const void* x, const uint32_t* w, const void* s, const voi
         if (!tc_shape_ok(M, N, K, bits)) return LQ_E_SHAPE;
         return finish(tc_run(x, w, s, b, outs[0], M, N, K, bits, dtype, cfg ? cfg->p : nullptr, st));
     }
-    if (!qmv_shape_ok(K, bits)) return LQ_E_SHAPE;
     const QmvMats mats = one_matrix(w, s, b, N);
+    if (fam == LQ_FAM_TCV) {
+        if (!tcv_shape_ok(M, K, bits)) return LQ_E_SHAPE;
+        return finish(tcv_run(x, M, mats, 1, N, K, nout, outs, a.seg_end, a.ldo, bits, dtype, cfg->p, st));
+    }
+    if (fam == LQ_FAM_AUTO && prefer_tcv(M, double(N) * K * bits / 8, K, bits)) {
+        rc = tcv_run(x, M, mats, 1, N, K, nout, outs, a.seg_end, a.ldo, bits, dtype, nullptr, st);
+        if (rc != LQ_E_SHAPE) return finish(rc);
+    }
+    if (!qmv_shape_ok(K, bits)) return LQ_E_SHAPE;
     return finish(qmv_run(x, M, mats, 1, a, bits, dtype, (cfg && fam == LQ_FAM_QMV) ? cfg->p : nullptr, M, 1, st));
 }
 
@@ -137,7 +158,6 @@ int lq_qmm_glu(const void* x, const uint32_t* w_gate, const void* s_gate, const 
     if (rc) return rc;
     if (!w_up || !s_up || !b_up || !h) return LQ_E_ARG;
     if (!aligned(w_up, 16) || !aligned(s_up, 4) || !aligned(b_up, 4)) return LQ_E_ALIGN;
-    if (!qmv_shape_ok(K, bits)) return LQ_E_SHAPE;
     QmvArgs a = {};
     a.M = M;
     a.N = I;
@@ -155,6 +175,18 @@ int lq_qmm_glu(const void* x, const uint32_t* w_gate, const void* s_gate, const 
     m.b[1] = b_up;
     m.rows_total[0] = m.rows_total[1] = I;
     const int fam = cfg ? cfg->family : LQ_FAM_AUTO;
+    void* outs[1] = {h};
+    if (fam == LQ_FAM_TCV) {
+        if (!tcv_shape_ok(M, K, bits)) return LQ_E_SHAPE;
+        return finish(tcv_run(x, M, m, 2, I, K, 1, outs, a.seg_end, a.ldo, bits, dtype, cfg->p,
+                              reinterpret_cast<cudaStream_t>(stream)));
+    }
+    if (fam == LQ_FAM_AUTO && prefer_tcv(M, 2.0 * I * K * bits / 8, K, bits)) {
+        rc = tcv_run(x, M, m, 2, I, K, 1, outs, a.seg_end, a.ldo, bits, dtype, nullptr,
+                     reinterpret_cast<cudaStream_t>(stream));
+        if (rc != LQ_E_SHAPE) return finish(rc);
+    }
+    if (!qmv_shape_ok(K, bits)) return LQ_E_SHAPE;
     return finish(qmv_run(x, M, m, 2, a, bits, dtype, (cfg && fam == LQ_FAM_QMV) ? cfg->p : nullptr, M, 1,
                           reinterpret_cast<cudaStream_t>(stream)));
 }

@@ -3,6 +3,7 @@
 #include "lq_host.cu"
 #include "quant.cu"
 #include "qmv.cu"
+#include "tcv.cu"
 #include "moe.cu"
 #include "tc_gemm.cu"
 #include "capi.cu"

@@ -1,0 +1,576 @@
+// Decode on the 5th-generation tensor cores (the "tcv" family): y (M <= 64 tokens) = x . dequant(w)^T.
+//
+// Per CTA: 128 weight rows (the MMA's M side) x a slice of K (split-K across a thread-block cluster);
+// tokens are the MMA's N side (16, 32 or 64 columns).
+//   * warp 12 streams the packed weight rows by TMA into a shared-memory ring, 128 bytes of each row per
+//     slot (four 64-wide groups at 4 bits, two at 8 bits: narrower boxes cost the TMA unit far more per
+//     byte and delay the x loads queued behind them);
+//     it starts before the previous kernel has finished (programmatic dependent launch), so a layer's
+//     weights are in flight while the layer before it still runs;
+//   * warps 0-7 dequantize one group per step -- each thread one weight row, 64 values -- straight
+//     into a tensor-memory ring with tcgen05.st (no shared-memory round trip for the bf16 weights);
+//   * warp 13 waits for the previous kernel and streams x's groups by TMA (SW128, the canonical
+//     K-major operand layout);
+//   * warps 8-11 (one per SM sub-partition) each issue the tcgen05.mma of every fourth group into
+//     their own accumulator: the per-issuer rate of small-N MMAs (~24 ns per M128xN16xK16 on B200)
+//     would otherwise bound the kernel, four issuers run ~3.4x faster;
+//   * warps 0-7 sum the accumulators, apply SwiGLU when gate and up rows are paired, and either store
+//     (one K slice) or reduce the cluster's partial sums through distributed shared memory.
+//
+// The dequantized weight is s*q + b rounded once to the activation dtype (the reference's dequantize
+// semantics, mlx quantized.h affine dequant), multiplied in the tensor core with fp32 accumulation.
+// Tensor memory: 256 columns per CTA. Shared memory per CTA is kept between 80 KB and half an SM, so
+// at most two CTAs share an SM and their allocations (2 x 256 of 512 columns) never wait.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <type_traits>
+
+#include "lq_host.h"
+#include "lq_ptx.cuh"
+#include "lq_status.cuh"
+#include "qmv.h"
+
+namespace lq {
+
+constexpr int TCV_THREADS = 448;  // 8 dequant warps, 4 MMA warps, weight producer, x producer
+constexpr int TCV_TMEM_COLS = 256;
+constexpr int TCV_MAX_SLOTS = 40;
+constexpr int TCV_MIN_SMEM = 80 * 1024;
+
+struct TcvArgs {
+    int M, N, K;
+    int G;         // K / 64 groups
+    int ks;        // K slices (cluster size along y)
+    int ws, xs;    // weight / x ring slots
+    int sbw;       // 32-bit words per row of the scale (and bias) table in shared memory (odd)
+    int w_bytes;   // bytes of the weight ring (also holds the partial sums at the end)
+    int row_off[2];
+    int rows_total[2];
+    const void* sptr[2];
+    const void* bptr[2];
+    void* out[3];
+    int seg_end[3];
+    int ldo[3];
+    int nseg_out;
+};
+
+template <int BITS, int NMAT, int NTOK>
+struct TcvShape {
+    static constexpr int GB = BITS * 8;     // bytes of one row of one group: 32 (4-bit) or 64 (8-bit)
+    static constexpr int GW = GB / 4;       // uint32 words of one row of one group
+    static constexpr int WG = 128 / GB;     // groups per weight slot (128 bytes of every row)
+    static constexpr int WSLOT = 128 * 128;  // one matrix, one slot, 128 rows of 128 bytes (SW128)
+    static constexpr int XSLOT = NTOK * 128;  // one group of x for NTOK tokens, SW128 rows of 128 bytes
+    static constexpr int NACC = NTOK <= 16 ? 4 : 2;  // MMA issuers = accumulators
+    static constexpr int DCOLS = NACC * NTOK;
+    static constexpr int AS = (TCV_TMEM_COLS - DCOLS) / 32;  // tensor-memory ring, one group (32 columns) each
+    static constexpr int RED_BYTES = NMAT * NTOK * 128 * 4;
+    static constexpr int CT = NTOK / 2 < 16 ? NTOK / 2 : 16;  // tokens per epilogue chunk of one warp
+};
+
+template <typename A>
+__device__ __forceinline__ void tcv_store(const A& a, int tok, int n, float v, bool bf16) {
+    int seg = 0, start = 0;
+    if (a.nseg_out > 1 && n >= a.seg_end[0]) {
+        seg = 1;
+        start = a.seg_end[0];
+        if (a.nseg_out > 2 && n >= a.seg_end[1]) {
+            seg = 2;
+            start = a.seg_end[1];
+        }
+    }
+    const size_t off = size_t(tok) * a.ldo[seg] + (n - start);
+    if (bf16)
+        reinterpret_cast<__nv_bfloat16*>(a.out[seg])[off] = __float2bfloat16_rn(v);
+    else
+        reinterpret_cast<__half*>(a.out[seg])[off] = __float2half_rn(v);
+}
+
+template <typename T>
+__device__ __forceinline__ float tcv_round(float v) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value)
+        return __bfloat162float(__float2bfloat16_rn(v));
+    else
+        return __half2float(__float2half_rn(v));
+}
+
+// silu(gate) * up with the activation-dtype rounding points of the reference's SwiGLU (gate and up
+// rounded, sigmoid rounded, silu rounded, product rounded by the store).
+template <typename T>
+__device__ __forceinline__ float tcv_swiglu(float g, float u) {
+    const float gt = tcv_round<T>(g), ut = tcv_round<T>(u);
+    const float sig = tcv_round<T>(1.0f / (1.0f + expf(-gt)));
+    return tcv_round<T>(gt * sig) * ut;
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]) {
+    if constexpr (N == 8)
+        tmem_ld_32x32b_x8(taddr, r);
+    else
+        tmem_ld_32x32b_x16(taddr, r);
+}
+
+// One weight row of one 64-wide group -> 32 packed pairs (k = 2j, 2j+1) in the activation dtype. The
+// row's 128 bytes in the slot are in the SW128 layout (16-byte chunk c stored at c ^ (row & 7)), which
+// keeps the warp's 32 row reads conflict-free; the group starts at chunk c0.
+template <typename T, int BITS>
+__device__ __forceinline__ void tcv_dequant_row(uint32_t rowp, int r, int c0, uint32_t s16, uint32_t b16,
+                                                uint32_t (&v)[32]) {
+    using TR = F16Traits<T>;
+    constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+    const int sw = r & 7;
+    if constexpr (BITS == 4) {
+        const uint4 u0 = lds128(rowp + (((c0 + 0) ^ sw) << 4));
+        const uint4 u1 = lds128(rowp + (((c0 + 1) ^ sw) << 4));
+        const uint32_t wd[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+        const uint32_t s2 = s16 | (s16 << 16), b2 = b16 | (b16 << 16);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t w = wd[j], w4 = w >> 4;
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                // code 2p is the low nibble of byte p of w, code 2p+1 the low nibble of byte p of w >> 4
+                const uint32_t sel = uint32_t(p) | (uint32_t(p) << 4) | (uint32_t(4 + p) << 8) | (uint32_t(p) << 12);
+                v[4 * j + p] = TR::sub_magic_fma(lop3_and_or(prmt(w, w4, sel), 0x000F000Fu, TR::kMagic2), s2, b2);
+            }
+        }
+    } else {
+        uint32_t wd[16];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint4 u = lds128(rowp + (((c0 + c) ^ sw) << 4));
+            wd[4 * c + 0] = u.x;
+            wd[4 * c + 1] = u.y;
+            wd[4 * c + 2] = u.z;
+            wd[4 * c + 3] = u.w;
+        }
+        if constexpr (kBF16) {
+            // a byte code as float: OR it into the mantissa of 2^23, subtract 2^23; s*q + b in fp32, one rounding
+            const float sf = TR::to_f32(s16), bf = TR::to_f32(b16);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                float f[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    f[i] = fmaf(__uint_as_float(prmt(wd[j], 0x4B000000u, 0x7540u + i)) - 8388608.0f, sf, bf);
+                v[2 * j] = cvt_bf16x2(f[1], f[0]);
+                v[2 * j + 1] = cvt_bf16x2(f[3], f[2]);
+            }
+        } else {
+            const uint32_t s2 = s16 | (s16 << 16), b2 = b16 | (b16 << 16);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                v[2 * j] = TR::sub_magic_fma(prmt(wd[j], 0x64646464u, 0x5140u), s2, b2);
+                v[2 * j + 1] = TR::sub_magic_fma(prmt(wd[j], 0x64646464u, 0x5342u), s2, b2);
+            }
+        }
+    }
+}
+
+// 64 registers: the register file is split across the four SM sub-partitions and a 14-warp CTA puts four
+// warps on some of them, so two CTAs per SM (one layer's CTA beside the next layer's) need <= 64.
+template <typename T, int BITS, int NMAT, int NTOK>
+__global__ void __maxnreg__(64)
+    tcv_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
+               const __grid_constant__ CUtensorMap tm_x, const TcvArgs a) {
+    using S = TcvShape<BITS, NMAT, NTOK>;
+    constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int WS = a.ws, XS = a.xs;
+    uint8_t* wring = smem;
+    uint8_t* xring = smem + a.w_bytes;
+    uint32_t* sbm = reinterpret_cast<uint32_t*>(xring + XS * S::XSLOT);
+    uint64_t* w_full = reinterpret_cast<uint64_t*>(sbm + NMAT * 2 * 128 * a.sbw);  // 256*sbw words: 8-byte aligned
+    uint64_t* w_empty = w_full + TCV_MAX_SLOTS;
+    uint64_t* x_full = w_empty + TCV_MAX_SLOTS;
+    uint64_t* x_empty = x_full + TCV_MAX_SLOTS;
+    uint64_t* a_full = x_empty + TCV_MAX_SLOTS;
+    uint64_t* a_empty = a_full + S::AS;
+    uint64_t* acc_full = a_empty + S::AS;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(acc_full + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n0 = blockIdx.x * 128;
+    const int rank = blockIdx.y;
+    const int pairs = a.G >> 1;
+    const int pb = rank * pairs / a.ks, pe = (rank + 1) * pairs / a.ks;
+    const int g_begin = 2 * pb, GC = 2 * (pe - pb);  // this CTA's groups
+    const int U = GC * NMAT;                         // dequant/MMA steps: (group, matrix)
+
+    if (tid == 0) {
+        for (int i = 0; i < WS; ++i) {
+            mbar_init(&w_full[i], 1);
+            mbar_init(&w_empty[i], 4 * NMAT * S::WG);  // every (group, matrix) step's four warps
+        }
+        for (int i = 0; i < XS; ++i) {
+            mbar_init(&x_full[i], 1);
+            mbar_init(&x_empty[i], NMAT);
+        }
+        for (int i = 0; i < S::AS; ++i) {
+            mbar_init(&a_full[i], 4);
+            mbar_init(&a_empty[i], 1);
+        }
+        mbar_init(acc_full, U < S::NACC ? (U > 0 ? U : 1) : S::NACC);
+        fence_barrier_init();
+    }
+    if (warp == 8) {
+        tmem_alloc(tslot, TCV_TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+    grid_dep_launch();
+
+    if (warp == 12) {
+        // ---- weight producer: every group of this CTA's K slice, ahead of everything else
+        if (lane == 0) {
+            prefetch_tmap(&tm_w0);
+            if (NMAT == 2) prefetch_tmap(&tm_w1);
+            const uint64_t pol = policy_evict_first();
+            const int NW = (GC + S::WG - 1) / S::WG;  // slots of this CTA's K slice (the last may be partial)
+            for (int wi = 0; wi < NW; ++wi) {
+                const int s = wi % WS;
+                if (wi >= WS) mbar_wait(&w_empty[s], ((wi / WS) - 1) & 1);
+                mbar_arrive_expect_tx(&w_full[s], NMAT * S::WSLOT);
+                const int kx = (g_begin + wi * S::WG) * S::GW;
+                tma_load_2d(wring + (s * NMAT) * S::WSLOT, &tm_w0, &w_full[s], kx, a.row_off[0] + n0, pol);
+                if (NMAT == 2)
+                    tma_load_2d(wring + (s * NMAT + 1) * S::WSLOT, &tm_w1, &w_full[s], kx, a.row_off[1] + n0, pol);
+            }
+            // drain: the last fill of every slot has landed before the CTA may exit
+            for (int s = 0; s < WS && s < NW; ++s) {
+                const int wl = s + WS * ((NW - 1 - s) / WS);
+                mbar_wait(&w_full[s], (wl / WS) & 1);
+            }
+        }
+    } else if (warp == 13) {
+        // ---- x producer: waits for the kernel that wrote x
+        if (lane == 0) {
+            prefetch_tmap(&tm_x);
+            grid_dep_wait();
+            const uint64_t pol = policy_evict_last();
+            for (int gi = 0; gi < GC; ++gi) {
+                const int s = gi % XS;
+                if (gi >= XS) mbar_wait(&x_empty[s], ((gi / XS) - 1) & 1);
+                mbar_arrive_expect_tx(&x_full[s], S::XSLOT);
+                tma_load_2d(xring + s * S::XSLOT, &tm_x, &x_full[s], (g_begin + gi) * 64, 0, pol);
+            }
+            for (int s = 0; s < XS && s < GC; ++s) {
+                const int gl = s + XS * ((GC - 1 - s) / XS);
+                mbar_wait(&x_full[s], (gl / XS) & 1);
+            }
+        }
+    } else if (warp >= 8) {
+        // ---- MMA issuers: issuer j takes steps j, j + NACC, ... into accumulator j
+        const int j = warp - 8;
+        if (j < S::NACC && lane == 0) {
+            const uint32_t idesc = umma_idesc_f16(kBF16 ? 1 : 0, 128, NTOK);
+            const uint64_t xd0 = umma_desc_sw128(smem_u32(xring));
+            const uint32_t dcol = tbase + uint32_t(j * NTOK);
+            for (int u = j; u < U; u += S::NACC) {
+                const int gi = u / NMAT, xs = gi % XS, au = u % S::AS;
+                mbar_wait(&a_full[au], (u / S::AS) & 1);
+                mbar_wait(&x_full[xs], (gi / XS) & 1);
+                tc_fence_after();
+                const uint32_t acol = tbase + uint32_t(S::DCOLS + au * 32);
+                const uint64_t xd = xd0 + uint64_t((xs * S::XSLOT) >> 4);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    tc_mma_ts(dcol, acol + 8 * kk, xd + 2 * kk, idesc, (u != j || kk != 0) ? 1u : 0u);
+                tc_commit(&a_empty[au]);
+                tc_commit(&x_empty[xs]);
+            }
+            if (j < U) tc_commit(acc_full);
+        }
+    } else {
+        // ---- dequant warps: quadrant q owns TMEM lanes / weight rows 32q..32q+31, half h takes every
+        // other step
+        const int q = warp & 3, h = warp >> 2;
+        const int r = 32 * q + lane;
+        {
+            // this CTA's scales and biases, one row per thread, into a [matrix][s|b][row][pair] table
+            const int npairs = GC >> 1;
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) {
+                const int grow = a.row_off[m] + n0 + r;
+                const bool ok = grow < a.rows_total[m];
+                const size_t off = ok ? (size_t(grow) * a.G + g_begin) * 2 : 0;
+                const char* sg = reinterpret_cast<const char*>(a.sptr[m]) + off;
+                const char* bg = reinterpret_cast<const char*>(a.bptr[m]) + off;
+                uint32_t* srow = sbm + ((m * 2 + 0) * 128 + r) * a.sbw;
+                uint32_t* brow = sbm + ((m * 2 + 1) * 128 + r) * a.sbw;
+                for (int w = h; w < npairs; w += 2) {
+                    cp_async(smem_u32(srow + w), sg + 4 * w, 4, ok);
+                    cp_async(smem_u32(brow + w), bg + 4 * w, 4, ok);
+                }
+            }
+            asm volatile("cp.async.wait_all;" ::: "memory");
+            named_barrier(1, 256);
+        }
+        const uint32_t trow = tbase + (uint32_t(32 * q) << 16);
+        for (int u = h; u < U; u += 2) {
+            const int gi = u / NMAT, m = u % NMAT;
+            const int wi = gi / S::WG, s = wi % WS, au = u % S::AS;
+            mbar_wait(&w_full[s], (wi / WS) & 1);
+            if (u >= S::AS) mbar_wait(&a_empty[au], ((u / S::AS) - 1) & 1);
+            tc_fence_after();
+            const uint32_t sw = sbm[((m * 2 + 0) * 128 + r) * a.sbw + (gi >> 1)];
+            const uint32_t bw = sbm[((m * 2 + 1) * 128 + r) * a.sbw + (gi >> 1)];
+            const uint32_t s16 = (gi & 1) ? (sw >> 16) : (sw & 0xFFFFu);
+            const uint32_t b16 = (gi & 1) ? (bw >> 16) : (bw & 0xFFFFu);
+            uint32_t v[32];
+            tcv_dequant_row<T, BITS>(smem_u32(wring + (s * NMAT + m) * S::WSLOT) + r * 128, r,
+                                     (gi % S::WG) * (S::GB / 16), s16, b16, v);
+            tmem_st_32x32b_x32(trow + uint32_t(S::DCOLS + au * 32), v);
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&a_full[au]);
+                mbar_arrive(&w_empty[s]);
+            }
+        }
+
+        // ---- epilogue: accumulators -> registers, summed per matrix
+        mbar_wait(acc_full, 0);
+        tc_fence_after();
+        const int n = n0 + r;
+        float* red = reinterpret_cast<float*>(wring);
+        constexpr int HT = NTOK / 2;
+#pragma unroll
+        for (int c = 0; c < HT / S::CT; ++c) {
+            const int t0 = h * HT + c * S::CT;
+            float acc[NMAT][S::CT];
+#pragma unroll
+            for (int mm = 0; mm < NMAT; ++mm)
+#pragma unroll
+                for (int t = 0; t < S::CT; ++t) acc[mm][t] = 0.0f;
+#pragma unroll
+            for (int jj = 0; jj < S::NACC; ++jj) {
+                if (jj >= U) break;
+                uint32_t rv[S::CT];
+                tmem_ld_cols<S::CT>(trow + uint32_t(jj * NTOK + t0), rv);
+                tmem_wait_ld();
+#pragma unroll
+                for (int t = 0; t < S::CT; ++t) acc[jj % NMAT][t] += __uint_as_float(rv[t]);
+            }
+            if (a.ks == 1) {
+                if (n < a.N) {
+#pragma unroll
+                    for (int t = 0; t < S::CT; ++t) {
+                        const int tok = t0 + t;
+                        if (tok >= a.M) break;
+                        float v0 = acc[0][t];
+                        if constexpr (NMAT == 2) v0 = tcv_swiglu<T>(v0, acc[1][t]);
+                        tcv_store(a, tok, n, v0, kBF16);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int mm = 0; mm < NMAT; ++mm)
+#pragma unroll
+                    for (int t = 0; t < S::CT; ++t) red[(mm * NTOK + t0 + t) * 128 + r] = acc[mm][t];
+            }
+        }
+    }
+
+    // tensor memory is free once every accumulator has been read
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 8) tmem_dealloc(tbase, TCV_TMEM_COLS);
+
+    if (a.ks > 1) {
+        // split-K: partial sums of the cluster's CTAs meet in distributed shared memory; CTA `rank`
+        // finishes rows [rank*128/ks, (rank+1)*128/ks) of the tile for every token
+        cluster_sync();
+        if (warp < 8) {
+            const float* red = reinterpret_cast<const float*>(wring);
+            const int r0 = rank * 128 / a.ks, r1 = (rank + 1) * 128 / a.ks, nr = r1 - r0;
+            const int total = a.M * nr;
+            for (int e = tid; e < total; e += 256) {
+                const int tok = e / nr, row = r0 + e % nr;
+                const int n = n0 + row;
+                float v[NMAT];
+#pragma unroll
+                for (int mm = 0; mm < NMAT; ++mm) v[mm] = 0.0f;
+                for (int p = 0; p < a.ks; ++p) {
+#pragma unroll
+                    for (int mm = 0; mm < NMAT; ++mm)
+                        v[mm] += ld_dsmem_f(map_peer(smem_u32(&red[(mm * NTOK + tok) * 128 + row]), uint32_t(p)));
+                }
+                if (n < a.N) {
+                    float v0 = v[0];
+                    if constexpr (NMAT == 2) v0 = tcv_swiglu<T>(v0, v[NMAT - 1]);
+                    tcv_store(a, tok, n, v0, kBF16);
+                }
+            }
+        }
+        cluster_sync();  // peers keep their shared memory until every CTA has read it
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+
+template <typename T, int BITS, int NMAT, int NTOK>
+static int tcv_launch_t(const void* x, int x_rows, const QmvMats& mats, TcvArgs a, int ks, int ws_req,
+                        cudaStream_t st) {
+    using S = TcvShape<BITS, NMAT, NTOK>;
+    const DeviceInfo& di = device_info();
+    const int pairs = a.G / 2;
+    if (ks < 1) ks = 1;
+    if (ks > 8) ks = 8;
+    if (ks > pairs) ks = pairs;
+    a.ks = ks;
+    const int gc_max = 2 * ((pairs + ks - 1) / ks);
+    a.sbw = (gc_max / 2) | 1;
+    const size_t sb_bytes = size_t(NMAT) * 2 * 128 * a.sbw * 4;
+    const size_t bar_bytes = (4 * TCV_MAX_SLOTS + 2 * S::AS + 1) * 8 + 16;
+    const size_t budget = di.smem_per_sm / 2 - 2048;
+    const int nw_max = (gc_max + S::WG - 1) / S::WG;
+    int ws = nw_max < TCV_MAX_SLOTS ? nw_max : TCV_MAX_SLOTS;
+    int xs = gc_max < TCV_MAX_SLOTS ? gc_max : TCV_MAX_SLOTS;
+    if (ws_req > 0 && ws_req < ws) ws = ws_req;
+    auto total = [&](int w, int x) {
+        size_t wb = size_t(w) * NMAT * S::WSLOT;
+        if (wb < size_t(S::RED_BYTES)) wb = S::RED_BYTES;
+        return wb + size_t(x) * S::XSLOT + sb_bytes + bar_bytes + 1024;
+    };
+    // weights first (their loads run ahead of the dependency), then x
+    while (total(ws, xs) > budget && xs > 4) --xs;
+    while (total(ws, xs) > budget && ws > 2) --ws;
+    while (total(ws, xs) > budget && xs > 2) --xs;
+    if (total(ws, xs) > budget) return LQ_E_SHAPE;
+    a.ws = ws;
+    a.xs = xs;
+    size_t wb = size_t(ws) * NMAT * S::WSLOT;
+    if (wb < size_t(S::RED_BYTES)) wb = S::RED_BYTES;
+    a.w_bytes = int(wb);
+    size_t smem = total(ws, xs);
+    if (smem < size_t(TCV_MIN_SMEM)) smem = TCV_MIN_SMEM;  // at most two CTAs per SM (tensor memory)
+
+    CUtensorMap tw[2], tx;
+    for (int m = 0; m < NMAT; ++m) {
+        const uint64_t wdims[2] = {uint64_t(a.K) * BITS / 32, uint64_t(mats.rows_total[m])};
+        const uint64_t wstr[1] = {uint64_t(a.K) * BITS / 8};
+        const uint32_t wbox[2] = {32, 128};
+        const int rc = make_tmap(&tw[m], CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, mats.w[m], wdims, wstr, wbox,
+                                 CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+        a.sptr[m] = mats.s[m];
+        a.bptr[m] = mats.b[m];
+        a.rows_total[m] = mats.rows_total[m];
+        a.row_off[m] = mats.row_off[m];
+    }
+    if (NMAT == 1) {
+        tw[1] = tw[0];
+        a.sptr[1] = a.sptr[0];
+        a.bptr[1] = a.bptr[0];
+        a.rows_total[1] = a.rows_total[0];
+        a.row_off[1] = a.row_off[0];
+    }
+    {
+        const uint64_t xdims[2] = {uint64_t(a.K), uint64_t(x_rows)};
+        const uint64_t xstr[1] = {uint64_t(a.K) * 2};
+        const uint32_t xbox[2] = {64, uint32_t(NTOK)};
+        const int rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, x, xdims, xstr, xbox,
+                                 CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
+
+    auto kern = tcv_kernel<T, BITS, NMAT, NTOK>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return LQ_E_CUDA;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((a.N + 127) / 128, ks, 1);
+    cfg.blockDim = dim3(TCV_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attrs[2];
+    int na = 0;
+    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+    if (ks > 1) {
+        attrs[na].id = cudaLaunchAttributeClusterDimension;
+        attrs[na].val.clusterDim.x = 1;
+        attrs[na].val.clusterDim.y = ks;
+        attrs[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    cfg.attrs = attrs;
+    cfg.numAttrs = na;
+    e = cudaLaunchKernelEx(&cfg, kern, tw[0], tw[1], tx, a);
+    return e == cudaSuccess ? LQ_OK : LQ_E_CUDA;
+}
+
+template <typename T, int BITS, int NMAT>
+static int tcv_dispatch_tok(int ntok, const void* x, int x_rows, const QmvMats& mats, const TcvArgs& a, int ks, int ws,
+                            cudaStream_t st) {
+    if (ntok == 16) return tcv_launch_t<T, BITS, NMAT, 16>(x, x_rows, mats, a, ks, ws, st);
+    if (ntok == 32) return tcv_launch_t<T, BITS, NMAT, 32>(x, x_rows, mats, a, ks, ws, st);
+    if (ntok == 64) return tcv_launch_t<T, BITS, NMAT, 64>(x, x_rows, mats, a, ks, ws, st);
+    return LQ_E_UNSUPPORTED;
+}
+
+// K slices for rb row tiles: about 1.3 CTAs per SM in total (measured on B200 over the fused QKV,
+// 8-bit gate/up and 8-bit down projections at 16-64 tokens: a kernel that holds tensor memory runs one CTA
+// per SM, and clusters of more than two CTAs do not pack every SM, so a second partial wave of smaller
+// slices beats one wave of large ones), at most 8 (portable cluster size).
+static int tcv_default_ks(int rb, int pairs, int sms) {
+    int ks = int(1.3 * sms / rb + 0.5);
+    if (ks < 1) ks = 1;
+    if (ks > 8) ks = 8;
+    if (ks > pairs) ks = pairs;
+    return ks;
+}
+
+bool tcv_shape_ok(int M, int K, int bits) {
+    if (M < 1 || M > 64) return false;
+    if (K < 128 || K % 128) return false;
+    return bits == 4 || bits == 8;
+}
+
+// p = {NTOK, KS, WS} (0 = choose).
+int tcv_run(const void* x, int M, const QmvMats& mats, int nmat, int N, int K, int nout, void* const* outs,
+            const int* seg_end, const int* ldo, int bits, int dtype, const int* p, cudaStream_t st) {
+    if (!tcv_shape_ok(M, K, bits)) return LQ_E_SHAPE;
+    TcvArgs a = {};
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.G = K / 64;
+    a.nseg_out = nout;
+    for (int i = 0; i < nout; ++i) {
+        a.out[i] = outs[i];
+        a.seg_end[i] = seg_end[i];
+        a.ldo[i] = ldo[i];
+    }
+    int ntok = p ? p[0] : 0, ks = p ? p[1] : 0, ws = p ? p[2] : 0;
+    if (ntok == 0) ntok = M <= 16 ? 16 : M <= 32 ? 32 : 64;
+    if (ntok < M) return LQ_E_ARG;
+    if (ks == 0) ks = tcv_default_ks((N + 127) / 128, a.G / 2, device_info().sm_count);
+    const bool bf16 = dtype == LQ_BF16;
+    if (bits == 4) {
+        if (nmat == 1)
+            return bf16 ? tcv_dispatch_tok<__nv_bfloat16, 4, 1>(ntok, x, M, mats, a, ks, ws, st)
+                        : tcv_dispatch_tok<__half, 4, 1>(ntok, x, M, mats, a, ks, ws, st);
+        return bf16 ? tcv_dispatch_tok<__nv_bfloat16, 4, 2>(ntok, x, M, mats, a, ks, ws, st)
+                    : tcv_dispatch_tok<__half, 4, 2>(ntok, x, M, mats, a, ks, ws, st);
+    }
+    if (nmat == 1)
+        return bf16 ? tcv_dispatch_tok<__nv_bfloat16, 8, 1>(ntok, x, M, mats, a, ks, ws, st)
+                    : tcv_dispatch_tok<__half, 8, 1>(ntok, x, M, mats, a, ks, ws, st);
+    return bf16 ? tcv_dispatch_tok<__nv_bfloat16, 8, 2>(ntok, x, M, mats, a, ks, ws, st)
+                : tcv_dispatch_tok<__half, 8, 2>(ntok, x, M, mats, a, ks, ws, st);
+}
+
+}  // namespace lq

@@ -11,6 +11,8 @@ every path is a hand-written sm_100a kernel of liblq.so:
 
 * ``("qmv", MT, WK, KS, NS)`` -- decode family (TMA-staged packed weights, register dequant into
   mma.sync fragments, cluster split-K), any M (weights streamed once per 64 rows);
+* ``("tcv", NTOK, KS, WS)`` -- decode on the tensor cores (weights dequantized into tensor memory as
+  the MMA's A operand, tokens as its N side, 16/32/64 columns), M <= 64, K % 128 == 0;
 * ``("tc", ...)`` -- prefill family (dequantized tiles in shared memory feeding tcgen05.mma with
   TMEM accumulators), M >= 128.
 
@@ -86,7 +88,7 @@ def dequantize(wq: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, gro
 
 # ---- matmul ------------------------------------------------------------------------------------
 
-_FAMILY = {"auto": _lib.FAM_AUTO, "qmv": _lib.FAM_QMV, "tc": _lib.FAM_TC}
+_FAMILY = {"auto": _lib.FAM_AUTO, "qmv": _lib.FAM_QMV, "tc": _lib.FAM_TC, "tcv": _lib.FAM_TCV}
 
 
 def _cfg(choice: Optional[Sequence]):
@@ -189,6 +191,11 @@ def candidates(M: int, K: int, N: int, bits: int = 4) -> list:
             for ks in (1, 2, 3, 4, 5, 8):
                 if ks <= nchunk:
                     out.append(("qmv", mt0, wk, ks, 0))
+        if K % 128 == 0:
+            out.append(("tcv", 0, 0, 0))
+            for ks in (1, 2, 3, 4, 6, 8):
+                if ks <= K // 128:
+                    out.append(("tcv", 0, ks, 0))
     if M >= PREFILL_M:
         out.append(("tc",))
     return out
