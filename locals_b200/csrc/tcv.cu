@@ -17,10 +17,15 @@
 //   * warps 0-7 sum the accumulators, apply SwiGLU when gate and up rows are paired, and either store
 //     (one K slice) or reduce the cluster's partial sums through distributed shared memory.
 //
+// Token tiles (grid z) of up to 256 columns make the same kernel a prefill GEMM in which every dequantized
+// weight feeds 256 tokens and never passes through shared memory.
+//
 // The dequantized weight is s*q + b rounded once to the activation dtype (the reference's dequantize
 // semantics, mlx quantized.h affine dequant), multiplied in the tensor core with fp32 accumulation.
-// Tensor memory: 256 columns per CTA. Shared memory per CTA is kept between 80 KB and half an SM, so
-// at most two CTAs share an SM and their allocations (2 x 256 of 512 columns) never wait.
+// Token tiles of up to 64 (decode) take 256 tensor-memory columns and at most half an SM's shared memory:
+// one launch places one CTA per SM (the occupancy calculator reports one block per SM for any kernel that
+// allocates tensor memory), but the next launch's CTAs can then start beside it and load their weights
+// while this launch still computes. Wider tiles (prefill) take all 512 columns and the opt-in shared memory.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -37,9 +42,8 @@
 namespace lq {
 
 constexpr int TCV_THREADS = 448;  // 8 dequant warps, 4 MMA warps, weight producer, x producer
-constexpr int TCV_TMEM_COLS = 256;
+
 constexpr int TCV_MAX_SLOTS = 40;
-constexpr int TCV_MIN_SMEM = 80 * 1024;
 
 struct TcvArgs {
     int M, N, K;
@@ -47,7 +51,7 @@ struct TcvArgs {
     int ks;        // K slices (cluster size along y)
     int ws, xs;    // weight / x ring slots
     int sbw;       // 32-bit words per row of the scale (and bias) table in shared memory (odd)
-    int w_bytes;   // bytes of the weight ring (also holds the partial sums at the end)
+    int w_bytes;   // bytes of the weight ring (with the x ring after it, also the split-K partial sums)
     int row_off[2];
     int rows_total[2];
     const void* sptr[2];
@@ -65,9 +69,12 @@ struct TcvShape {
     static constexpr int WG = 128 / GB;     // groups per weight slot (128 bytes of every row)
     static constexpr int WSLOT = 128 * 128;  // one matrix, one slot, 128 rows of 128 bytes (SW128)
     static constexpr int XSLOT = NTOK * 128;  // one group of x for NTOK tokens, SW128 rows of 128 bytes
-    static constexpr int NACC = NTOK <= 16 ? 4 : 2;  // MMA issuers = accumulators
+    // MMA issuers = accumulators: small-N MMAs are bound by the issue rate of one thread (~24 ns each on
+    // B200), so narrow token tiles spread them over several issuing warps; a multiple of NMAT
+    static constexpr int NACC = NTOK <= 16 ? 4 : (NTOK <= 64 || NMAT == 2) ? 2 : 1;
+    static constexpr int TMEM_COLS = NTOK <= 64 ? 256 : 512;
     static constexpr int DCOLS = NACC * NTOK;
-    static constexpr int AS = (TCV_TMEM_COLS - DCOLS) / 32;  // tensor-memory ring, one group (32 columns) each
+    static constexpr int AS = (TMEM_COLS - DCOLS) / 32;  // tensor-memory ring, one group (32 columns) each
     static constexpr int RED_BYTES = NMAT * NTOK * 128 * 4;
     static constexpr int CT = NTOK / 2 < 16 ? NTOK / 2 : 16;  // tokens per epilogue chunk of one warp
 };
@@ -172,10 +179,8 @@ __device__ __forceinline__ void tcv_dequant_row(uint32_t rowp, int r, int c0, ui
     }
 }
 
-// 64 registers: the register file is split across the four SM sub-partitions and a 14-warp CTA puts four
-// warps on some of them, so two CTAs per SM (one layer's CTA beside the next layer's) need <= 64.
 template <typename T, int BITS, int NMAT, int NTOK>
-__global__ void __maxnreg__(64)
+__global__ void __launch_bounds__(TCV_THREADS, 1)
     tcv_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
                const __grid_constant__ CUtensorMap tm_x, const TcvArgs a) {
     using S = TcvShape<BITS, NMAT, NTOK>;
@@ -199,6 +204,8 @@ __global__ void __maxnreg__(64)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n0 = blockIdx.x * 128;
     const int rank = blockIdx.y;
+    const int tok0 = blockIdx.z * NTOK;                            // first token of this tile
+    const int mt = a.M - tok0 < NTOK ? a.M - tok0 : NTOK;          // tokens of this tile
     const int pairs = a.G >> 1;
     const int pb = rank * pairs / a.ks, pe = (rank + 1) * pairs / a.ks;
     const int g_begin = 2 * pb, GC = 2 * (pe - pb);  // this CTA's groups
@@ -221,7 +228,7 @@ __global__ void __maxnreg__(64)
         fence_barrier_init();
     }
     if (warp == 8) {
-        tmem_alloc(tslot, TCV_TMEM_COLS);
+        tmem_alloc(tslot, S::TMEM_COLS);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -230,49 +237,55 @@ __global__ void __maxnreg__(64)
     const uint32_t tbase = *tslot;
     grid_dep_launch();
 
+    // Producer and MMA roles run their loops with the whole warp (one lane issues): a lone lane whose warp
+    // mates already wait at the CTA barrier below is scheduled so rarely that its TMAs and MMAs trickle out.
     if (warp == 12) {
-        // ---- weight producer: every group of this CTA's K slice, ahead of everything else
+        // ---- weight producer: every slot of this CTA's K slice, ahead of everything else
         if (lane == 0) {
             prefetch_tmap(&tm_w0);
             if (NMAT == 2) prefetch_tmap(&tm_w1);
-            const uint64_t pol = policy_evict_first();
-            const int NW = (GC + S::WG - 1) / S::WG;  // slots of this CTA's K slice (the last may be partial)
-            for (int wi = 0; wi < NW; ++wi) {
-                const int s = wi % WS;
-                if (wi >= WS) mbar_wait(&w_empty[s], ((wi / WS) - 1) & 1);
+        }
+        const uint64_t pol = policy_evict_first();
+        const int NW = (GC + S::WG - 1) / S::WG;  // slots of this CTA's K slice (the last may be partial)
+        for (int wi = 0; wi < NW; ++wi) {
+            const int s = wi % WS;
+            if (wi >= WS) mbar_wait(&w_empty[s], ((wi / WS) - 1) & 1);
+            if (lane == 0) {
                 mbar_arrive_expect_tx(&w_full[s], NMAT * S::WSLOT);
                 const int kx = (g_begin + wi * S::WG) * S::GW;
                 tma_load_2d(wring + (s * NMAT) * S::WSLOT, &tm_w0, &w_full[s], kx, a.row_off[0] + n0, pol);
                 if (NMAT == 2)
                     tma_load_2d(wring + (s * NMAT + 1) * S::WSLOT, &tm_w1, &w_full[s], kx, a.row_off[1] + n0, pol);
             }
-            // drain: the last fill of every slot has landed before the CTA may exit
-            for (int s = 0; s < WS && s < NW; ++s) {
-                const int wl = s + WS * ((NW - 1 - s) / WS);
-                mbar_wait(&w_full[s], (wl / WS) & 1);
-            }
+            __syncwarp();
+        }
+        // drain: the last fill of every slot has landed before the CTA may exit
+        for (int s = 0; s < WS && s < NW; ++s) {
+            const int wl = s + WS * ((NW - 1 - s) / WS);
+            mbar_wait(&w_full[s], (wl / WS) & 1);
         }
     } else if (warp == 13) {
         // ---- x producer: waits for the kernel that wrote x
-        if (lane == 0) {
-            prefetch_tmap(&tm_x);
-            grid_dep_wait();
-            const uint64_t pol = policy_evict_last();
-            for (int gi = 0; gi < GC; ++gi) {
-                const int s = gi % XS;
-                if (gi >= XS) mbar_wait(&x_empty[s], ((gi / XS) - 1) & 1);
+        if (lane == 0) prefetch_tmap(&tm_x);
+        grid_dep_wait();
+        const uint64_t pol = policy_evict_last();
+        for (int gi = 0; gi < GC; ++gi) {
+            const int s = gi % XS;
+            if (gi >= XS) mbar_wait(&x_empty[s], ((gi / XS) - 1) & 1);
+            if (lane == 0) {
                 mbar_arrive_expect_tx(&x_full[s], S::XSLOT);
-                tma_load_2d(xring + s * S::XSLOT, &tm_x, &x_full[s], (g_begin + gi) * 64, 0, pol);
+                tma_load_2d(xring + s * S::XSLOT, &tm_x, &x_full[s], (g_begin + gi) * 64, tok0, pol);
             }
-            for (int s = 0; s < XS && s < GC; ++s) {
-                const int gl = s + XS * ((GC - 1 - s) / XS);
-                mbar_wait(&x_full[s], (gl / XS) & 1);
-            }
+            __syncwarp();
+        }
+        for (int s = 0; s < XS && s < GC; ++s) {
+            const int gl = s + XS * ((GC - 1 - s) / XS);
+            mbar_wait(&x_full[s], (gl / XS) & 1);
         }
     } else if (warp >= 8) {
         // ---- MMA issuers: issuer j takes steps j, j + NACC, ... into accumulator j
         const int j = warp - 8;
-        if (j < S::NACC && lane == 0) {
+        if (j < S::NACC) {
             const uint32_t idesc = umma_idesc_f16(kBF16 ? 1 : 0, 128, NTOK);
             const uint64_t xd0 = umma_desc_sw128(smem_u32(xring));
             const uint32_t dcol = tbase + uint32_t(j * NTOK);
@@ -281,15 +294,19 @@ __global__ void __maxnreg__(64)
                 mbar_wait(&a_full[au], (u / S::AS) & 1);
                 mbar_wait(&x_full[xs], (gi / XS) & 1);
                 tc_fence_after();
-                const uint32_t acol = tbase + uint32_t(S::DCOLS + au * 32);
-                const uint64_t xd = xd0 + uint64_t((xs * S::XSLOT) >> 4);
+                if (lane == 0) {
+                    const uint32_t acol = tbase + uint32_t(S::DCOLS + au * 32);
+                    const uint64_t xd = xd0 + uint64_t((xs * S::XSLOT) >> 4);
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    tc_mma_ts(dcol, acol + 8 * kk, xd + 2 * kk, idesc, (u != j || kk != 0) ? 1u : 0u);
-                tc_commit(&a_empty[au]);
-                tc_commit(&x_empty[xs]);
+                    for (int kk = 0; kk < 4; ++kk)
+                        tc_mma_ts(dcol, acol + 8 * kk, xd + 2 * kk, idesc, (u != j || kk != 0) ? 1u : 0u);
+                    tc_commit(&a_empty[au]);
+                    tc_commit(&x_empty[xs]);
+                }
+                __syncwarp();
             }
-            if (j < U) tc_commit(acc_full);
+            if (j < U && lane == 0) tc_commit(acc_full);
+            __syncwarp();
         }
     } else {
         // ---- dequant warps: quadrant q owns TMEM lanes / weight rows 32q..32q+31, half h takes every
@@ -368,10 +385,10 @@ __global__ void __maxnreg__(64)
 #pragma unroll
                     for (int t = 0; t < S::CT; ++t) {
                         const int tok = t0 + t;
-                        if (tok >= a.M) break;
+                        if (tok >= mt) break;
                         float v0 = acc[0][t];
                         if constexpr (NMAT == 2) v0 = tcv_swiglu<T>(v0, acc[1][t]);
-                        tcv_store(a, tok, n, v0, kBF16);
+                        tcv_store(a, tok0 + tok, n, v0, kBF16);
                     }
                 }
             } else {
@@ -386,7 +403,7 @@ __global__ void __maxnreg__(64)
     // tensor memory is free once every accumulator has been read
     tc_fence_before();
     __syncthreads();
-    if (warp == 8) tmem_dealloc(tbase, TCV_TMEM_COLS);
+    if (warp == 8) tmem_dealloc(tbase, S::TMEM_COLS);
 
     if (a.ks > 1) {
         // split-K: partial sums of the cluster's CTAs meet in distributed shared memory; CTA `rank`
@@ -395,7 +412,7 @@ __global__ void __maxnreg__(64)
         if (warp < 8) {
             const float* red = reinterpret_cast<const float*>(wring);
             const int r0 = rank * 128 / a.ks, r1 = (rank + 1) * 128 / a.ks, nr = r1 - r0;
-            const int total = a.M * nr;
+            const int total = mt * nr;
             for (int e = tid; e < total; e += 256) {
                 const int tok = e / nr, row = r0 + e % nr;
                 const int n = n0 + row;
@@ -410,7 +427,7 @@ __global__ void __maxnreg__(64)
                 if (n < a.N) {
                     float v0 = v[0];
                     if constexpr (NMAT == 2) v0 = tcv_swiglu<T>(v0, v[NMAT - 1]);
-                    tcv_store(a, tok, n, v0, kBF16);
+                    tcv_store(a, tok0 + tok, n, v0, kBF16);
                 }
             }
         }
@@ -434,16 +451,20 @@ static int tcv_launch_t(const void* x, int x_rows, const QmvMats& mats, TcvArgs 
     a.sbw = (gc_max / 2) | 1;
     const size_t sb_bytes = size_t(NMAT) * 2 * 128 * a.sbw * 4;
     const size_t bar_bytes = (4 * TCV_MAX_SLOTS + 2 * S::AS + 1) * 8 + 16;
-    const size_t budget = di.smem_per_sm / 2 - 2048;
+    const size_t budget = NTOK <= 64 ? di.smem_per_sm / 2 - 2048 : di.smem_optin - 1024;
     const int nw_max = (gc_max + S::WG - 1) / S::WG;
     int ws = nw_max < TCV_MAX_SLOTS ? nw_max : TCV_MAX_SLOTS;
     int xs = gc_max < TCV_MAX_SLOTS ? gc_max : TCV_MAX_SLOTS;
     if (ws_req > 0 && ws_req < ws) ws = ws_req;
-    auto total = [&](int w, int x) {
+    // the split-K partial sums (ks > 1) overlay the weight and x rings, idle by then
+    const size_t red = ks > 1 ? size_t(S::RED_BYTES) : 0;
+    auto ring_bytes = [&](int w, int x) {
         size_t wb = size_t(w) * NMAT * S::WSLOT;
-        if (wb < size_t(S::RED_BYTES)) wb = S::RED_BYTES;
-        return wb + size_t(x) * S::XSLOT + sb_bytes + bar_bytes + 1024;
+        const size_t xb = size_t(x) * S::XSLOT;
+        if (wb + xb < red) wb = (red - xb + 1023) / 1024 * 1024;
+        return wb;
     };
+    auto total = [&](int w, int x) { return ring_bytes(w, x) + size_t(x) * S::XSLOT + sb_bytes + bar_bytes + 1024; };
     // weights first (their loads run ahead of the dependency), then x
     while (total(ws, xs) > budget && xs > 4) --xs;
     while (total(ws, xs) > budget && ws > 2) --ws;
@@ -451,11 +472,8 @@ static int tcv_launch_t(const void* x, int x_rows, const QmvMats& mats, TcvArgs 
     if (total(ws, xs) > budget) return LQ_E_SHAPE;
     a.ws = ws;
     a.xs = xs;
-    size_t wb = size_t(ws) * NMAT * S::WSLOT;
-    if (wb < size_t(S::RED_BYTES)) wb = S::RED_BYTES;
-    a.w_bytes = int(wb);
-    size_t smem = total(ws, xs);
-    if (smem < size_t(TCV_MIN_SMEM)) smem = TCV_MIN_SMEM;  // at most two CTAs per SM (tensor memory)
+    a.w_bytes = int(ring_bytes(ws, xs));
+    const size_t smem = total(ws, xs);
 
     CUtensorMap tw[2], tx;
     for (int m = 0; m < NMAT; ++m) {
@@ -490,7 +508,7 @@ static int tcv_launch_t(const void* x, int x_rows, const QmvMats& mats, TcvArgs 
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return LQ_E_CUDA;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((a.N + 127) / 128, ks, 1);
+    cfg.gridDim = dim3((a.N + 127) / 128, ks, (a.M + NTOK - 1) / NTOK);
     cfg.blockDim = dim3(TCV_THREADS, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
@@ -518,6 +536,10 @@ static int tcv_dispatch_tok(int ntok, const void* x, int x_rows, const QmvMats& 
     if (ntok == 16) return tcv_launch_t<T, BITS, NMAT, 16>(x, x_rows, mats, a, ks, ws, st);
     if (ntok == 32) return tcv_launch_t<T, BITS, NMAT, 32>(x, x_rows, mats, a, ks, ws, st);
     if (ntok == 64) return tcv_launch_t<T, BITS, NMAT, 64>(x, x_rows, mats, a, ks, ws, st);
+    if (ntok == 128) return tcv_launch_t<T, BITS, NMAT, 128>(x, x_rows, mats, a, ks, ws, st);
+    if constexpr (NMAT == 1) {
+        if (ntok == 256) return tcv_launch_t<T, BITS, NMAT, 256>(x, x_rows, mats, a, ks, ws, st);
+    }
     return LQ_E_UNSUPPORTED;
 }
 
@@ -534,7 +556,7 @@ static int tcv_default_ks(int rb, int pairs, int sms) {
 }
 
 bool tcv_shape_ok(int M, int K, int bits) {
-    if (M < 1 || M > 64) return false;
+    if (M < 1) return false;
     if (K < 128 || K % 128) return false;
     return bits == 4 || bits == 8;
 }
@@ -555,9 +577,9 @@ int tcv_run(const void* x, int M, const QmvMats& mats, int nmat, int N, int K, i
         a.ldo[i] = ldo[i];
     }
     int ntok = p ? p[0] : 0, ks = p ? p[1] : 0, ws = p ? p[2] : 0;
-    if (ntok == 0) ntok = M <= 16 ? 16 : M <= 32 ? 32 : 64;
-    if (ntok < M) return LQ_E_ARG;
-    if (ks == 0) ks = tcv_default_ks((N + 127) / 128, a.G / 2, device_info().sm_count);
+    if (ntok == 0) ntok = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 || nmat == 2 ? 128 : 256;
+    if (ntok != 16 && ntok != 32 && ntok != 64 && ntok != 128 && ntok != 256) return LQ_E_ARG;
+    if (ks == 0) ks = tcv_default_ks((N + 127) / 128 * ((M + ntok - 1) / ntok), a.G / 2, device_info().sm_count);
     const bool bf16 = dtype == LQ_BF16;
     if (bits == 4) {
         if (nmat == 1)

@@ -50,12 +50,15 @@ def test_tc_tilings_agree(cuda, bn):
     assert rel_err(y.float().cpu().numpy(), ref) <= TOL_REL
 
 
-def test_tc_config5_full(cuda):
+@pytest.mark.parametrize("choice", [("tc",), ("tcv", 256, 0, 0)])
+def test_tc_config5_full(cuda, choice):
+    # both prefill formulations: x on the MMA's M side (tc), and weights dequantized into tensor memory
+    # with 256-token tiles on N (tcv)
     import torch
     from locals_b200 import kernels
 
     M, N, K = 2048, 14336, 4096
-    x, q, y = _tc(cuda, M, N, K, 4, "bfloat16", seed=4)
+    x, q, y = _tc(cuda, M, N, K, 4, "bfloat16", seed=4, choice=choice)
     # sampled rows against the oracle
     rows = np.array([0, 1, 127, 128, 1000, 2047])
     ref = O.round_to(O.qmm(x[rows], *q), "bfloat16")

@@ -71,6 +71,20 @@ def test_tcv_every_tiling(cuda, choice):
     assert rel_err(y, ref) <= TOL_REL
 
 
+# token tiles past 64 tokens: 128- and 256-token tiles on grid z, a ragged last tile, both dtypes
+@pytest.mark.parametrize("M,N,K,bits,dtype,ntok", [
+    (100, 520, 768, 4, "bfloat16", 0),
+    (300, 384, 1024, 4, "float16", 0),
+    (130, 272, 512, 8, "bfloat16", 0),
+    (513, 256, 640, 4, "bfloat16", 256),
+    (200, 300, 1024, 8, "float16", 128),
+    (70, 136, 2048, 4, "bfloat16", 16),
+])
+def test_tcv_token_tiles(cuda, M, N, K, bits, dtype, ntok):
+    y, ref = _run(cuda, M, N, K, bits, dtype, seed=M + N * 7 + K, choice=("tcv", ntok, 0, 0))
+    assert rel_err(y, ref) <= TOL_REL
+
+
 def test_tcv_split_and_glu(cuda):
     # the fused QKV split into three outputs and the fused gate/up SwiGLU on the tensor-core family
     import torch
@@ -88,7 +102,8 @@ def test_tcv_split_and_glu(cuda):
     got = np.concatenate([o.float().cpu().numpy() for o in outs], axis=1)
     assert rel_err(got, ref) <= TOL_REL
 
-    for bits, I in ((4, 384), (8, 200)):
+    for bits, I, M in ((4, 384, 7), (8, 200, 7), (4, 256, 200)):
+        x = act(rng, M, K, "bfloat16")
         gq, gs, gb = qweights(rng, I, K, bits, "bfloat16")
         uq, us, ub = qweights(rng, I, K, bits, "bfloat16")
         g = O.round_to(O.qmm(x, gq, gs, gb, 64, bits), "bfloat16")
