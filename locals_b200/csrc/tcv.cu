@@ -74,7 +74,8 @@ struct TcvShape {
     static constexpr int NACC = NTOK <= 16 ? 4 : (NTOK <= 64 || NMAT == 2) ? 2 : 1;
     static constexpr int TMEM_COLS = NTOK <= 64 ? 256 : 512;
     static constexpr int DCOLS = NACC * NTOK;
-    static constexpr int AS = (TMEM_COLS - DCOLS) / 32;  // tensor-memory ring, one group (32 columns) each
+    static constexpr int AS = (TMEM_COLS - DCOLS) / 32;
+    static_assert(AS >= 2 && DCOLS + 32 * AS <= TMEM_COLS, "accumulators and A ring exceed the TMEM allocation");  // tensor-memory ring, one group (32 columns) each
     static constexpr int RED_BYTES = NMAT * NTOK * 128 * 4;
     static constexpr int CT = NTOK / 2 < 16 ? NTOK / 2 : 16;  // tokens per epilogue chunk of one warp
 };
