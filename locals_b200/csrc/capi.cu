@@ -33,6 +33,9 @@ bool tc_shape_ok(int M, int N, int K, int bits);
 bool tcv_shape_ok(int M, int K, int bits);
 int tcv_run(const void* x, int M, const QmvMats& mats, int nmat, int N, int K, int nout, void* const* outs,
             const int* seg_end, const int* ldo, int bits, int dtype, const int* p, cudaStream_t st);
+int tcv_run_grouped(const void* xs, int P, const QmvMats& mats, int nmat, int N, int K, void* out,
+                    const int32_t* starts, const int32_t* experts, const int32_t* nseg, int E, int bits, int dtype,
+                    const int* p, cudaStream_t st);
 }  // namespace lq
 
 using namespace lq;
@@ -301,6 +304,12 @@ int lq_moe_experts(const void* xs, const int32_t* starts, const int32_t* experts
     m.b[1] = glu ? b1 : b0;
     m.rows_total[0] = m.rows_total[1] = E * N;
     if (gather_order && gather_k < 1) return LQ_E_ARG;
+    // from 128 routed rows the expert GEMMs run on the tensor-core family (pre-gathered rows only)
+    if (!gather_order && P >= 128 && tcv_shape_ok(P, K, bits)) {
+        rc = tcv_run_grouped(xs, P, m, glu ? 2 : 1, N, K, out, starts, experts, nseg, E, bits, dtype, nullptr,
+                             reinterpret_cast<cudaStream_t>(stream));
+        if (rc != LQ_E_SHAPE) return finish(rc);
+    }
     a.gather = gather_order;
     a.gather_k = gather_k;
     const int nseg_grid = (E + 1) < P ? (E + 1) : P;  // (one more for a padding bucket, expert id E)

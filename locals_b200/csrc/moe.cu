@@ -166,13 +166,21 @@ __global__ void route_topk_kernel(const float* logits, int T, int E, int k, int 
 }
 
 // One CTA of 1024 threads. order/starts/experts/nseg as lq_moe_group; pos = inverse of order (optional).
+constexpr int GROUP_STAGE = 8192;  // routed pairs staged in shared memory per ranking pass
+
+// Stable counting sort of the routed (token, slot) pairs by expert (moe_kernel.group's order): a shared-memory
+// histogram, a one-warp scan that emits the segments, then a one-warp pass over the pairs in order, 32 at a
+// time: __match_any_sync finds the lanes of the same expert, a pair's rank is the expert's running count
+// plus its rank among those lanes.
 __global__ void group_kernel(const uint32_t* inds, int P, int E, int32_t* order, int32_t* starts, int32_t* experts,
                              int32_t* nseg, int32_t* pos) {
     grid_dep_wait();
     grid_dep_launch();
     extern __shared__ int32_t sh[];
-    int32_t* cnt = sh;       // E
-    int32_t* base = sh + E;  // E
+    int32_t* cnt = sh;                                   // E counts
+    int32_t* run = sh + E;                               // E running positions
+    uint32_t* staged = reinterpret_cast<uint32_t*>(sh + 2 * E);  // GROUP_STAGE expert ids
+    const int lane = threadIdx.x & 31;
     for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
     for (int p = threadIdx.x; p < P; p += blockDim.x) {
@@ -183,30 +191,54 @@ __global__ void group_kernel(const uint32_t* inds, int P, int E, int32_t* order,
             record_status(LQ_DEV_BOUNDS);
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (threadIdx.x < 32) {
         int at = 0, s = 0;
-        for (int e = 0; e < E; ++e) {
-            base[e] = at;
-            if (cnt[e] > 0) {
-                starts[s] = at;
-                experts[s] = e;
-                ++s;
+        for (int c = 0; c < E; c += 32) {
+            const int e = c + lane;
+            const int v = e < E ? cnt[e] : 0;
+            int incl = v;
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+                const int t = __shfl_up_sync(0xFFFFFFFFu, incl, d);
+                if (lane >= d) incl += t;
             }
-            at += cnt[e];
+            const unsigned nz = __ballot_sync(0xFFFFFFFFu, v > 0);
+            if (e < E) run[e] = at + incl - v;
+            if (v > 0) {
+                const int si = s + __popc(nz & ((1u << lane) - 1u));
+                starts[si] = at + incl - v;
+                experts[si] = e;
+            }
+            at += __shfl_sync(0xFFFFFFFFu, incl, 31);
+            s += __popc(nz);
         }
-        starts[s] = at;
-        nseg[0] = s;
+        if (lane == 0) {
+            starts[s] = at;
+            nseg[0] = s;
+        }
     }
-    __syncthreads();
-    // stable placement: rank of p among the pairs of its expert = pairs q < p with the same expert
-    for (int p = threadIdx.x; p < P; p += blockDim.x) {
-        const uint32_t e = inds[p];
-        if (e >= uint32_t(E)) continue;
-        int rank = 0;
-        for (int q = 0; q < p; ++q) rank += (inds[q] == e) ? 1 : 0;
-        const int j = base[e] + rank;
-        order[j] = p;
-        if (pos) pos[p] = j;
+    for (int p0 = 0; p0 < P; p0 += GROUP_STAGE) {
+        const int n = P - p0 < GROUP_STAGE ? P - p0 : GROUP_STAGE;
+        __syncthreads();
+        for (int i = threadIdx.x; i < n; i += blockDim.x) staged[i] = inds[p0 + i];
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            for (int c = 0; c < n; c += 32) {
+                const int i = c + lane;
+                const uint32_t e = i < n ? staged[i] : 0xFFFFFFFFu;
+                const bool valid = e < uint32_t(E);
+                const unsigned peers = __match_any_sync(0xFFFFFFFFu, valid ? e : 0xFFFFFFFFu);
+                const int rank = __popc(peers & ((1u << lane) - 1u));
+                const int j = valid ? run[e] + rank : 0;
+                __syncwarp();
+                if (valid && rank == 0) run[e] += __popc(peers);
+                __syncwarp();
+                if (valid) {
+                    order[j] = p0 + i;
+                    if (pos) pos[p0 + i] = j;
+                }
+            }
+        }
     }
 }
 
@@ -337,7 +369,7 @@ int route_topk_run(const float* logits, int T, int E, int k, int mode, uint32_t*
 
 int group_run(const uint32_t* inds, int P, int E, int32_t* order, int32_t* starts, int32_t* experts, int32_t* nseg,
               int32_t* pos, cudaStream_t st) {
-    const size_t smem = size_t(2) * E * sizeof(int32_t);
+    const size_t smem = size_t(2) * E * sizeof(int32_t) + size_t(GROUP_STAGE) * sizeof(uint32_t);
     if (smem > 48 * 1024) {
         const cudaError_t e = cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
         if (e != cudaSuccess) return LQ_E_CUDA;

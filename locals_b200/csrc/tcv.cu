@@ -60,6 +60,14 @@ struct TcvArgs {
     int seg_end[3];
     int ldo[3];
     int nseg_out;
+    // grouped mode (MoE experts): grid z walks token tiles of the expert segments of a counting sort
+    // (rows starts[s] .. starts[s+1] of x, expert experts[s], weights at row experts[s] * N of stacked
+    // (E, N, ...) arrays); expert id n_experts is the padding bucket, skipped
+    int grouped;
+    const int32_t* starts;
+    const int32_t* experts;
+    const int32_t* nseg;
+    int n_experts;
 };
 
 template <int BITS, int NMAT, int NTOK>
@@ -74,8 +82,8 @@ struct TcvShape {
     static constexpr int NACC = NTOK <= 16 ? 4 : (NTOK <= 64 || NMAT == 2) ? 2 : 1;
     static constexpr int TMEM_COLS = NTOK <= 64 ? 256 : 512;
     static constexpr int DCOLS = NACC * NTOK;
-    static constexpr int AS = (TMEM_COLS - DCOLS) / 32;
-    static_assert(AS >= 2 && DCOLS + 32 * AS <= TMEM_COLS, "accumulators and A ring exceed the TMEM allocation");  // tensor-memory ring, one group (32 columns) each
+    static constexpr int AS = (TMEM_COLS - DCOLS) / 32;  // tensor-memory A ring, one group (32 columns) each
+    static_assert(AS >= 2 && DCOLS + 32 * AS <= TMEM_COLS, "accumulators and A ring exceed the TMEM allocation");
     static constexpr int RED_BYTES = NMAT * NTOK * 128 * 4;
     static constexpr int CT = NTOK / 2 < 16 ? NTOK / 2 : 16;  // tokens per epilogue chunk of one warp
 };
@@ -205,8 +213,58 @@ __global__ void __launch_bounds__(TCV_THREADS, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n0 = blockIdx.x * 128;
     const int rank = blockIdx.y;
-    const int tok0 = blockIdx.z * NTOK;                            // first token of this tile
-    const int mt = a.M - tok0 < NTOK ? a.M - tok0 : NTOK;          // tokens of this tile
+    int tok0 = blockIdx.z * NTOK;                     // first x row of this tile
+    int mt = a.M - tok0 < NTOK ? a.M - tok0 : NTOK;   // rows of this tile
+    int wrow = 0;                                     // first weight row of this tile's matrix
+    if (a.grouped) {
+        // segments come from the grouping kernel; tile z of the concatenated per-segment tile lists
+        grid_dep_wait();
+        int* tile_info = reinterpret_cast<int*>(smem_raw);  // (before anything else uses shared memory)
+        if (warp == 0) {
+            const int ns = a.nseg[0];
+            const int z = blockIdx.z;
+            int base = 0, seg = -1, tile = 0;
+            for (int c = 0; c < ns; c += 32) {
+                const int sg = c + lane;
+                int t = 0;
+                if (sg < ns) {
+                    const int e = a.experts[sg], r = a.starts[sg + 1] - a.starts[sg];
+                    if (e < 0 || e > a.n_experts || r < 0) record_status(LQ_DEV_BOUNDS);
+                    else if (e < a.n_experts) t = (r + NTOK - 1) / NTOK;
+                }
+                int incl = t;
+#pragma unroll
+                for (int d = 1; d < 32; d <<= 1) {
+                    const int v = __shfl_up_sync(0xFFFFFFFFu, incl, d);
+                    if (lane >= d) incl += v;
+                }
+                const bool mine = z >= base + incl - t && z < base + incl;
+                const unsigned hit = __ballot_sync(0xFFFFFFFFu, mine);
+                if (hit) {
+                    const int l = __ffs(hit) - 1;
+                    seg = __shfl_sync(0xFFFFFFFFu, sg, l);
+                    tile = z - base - __shfl_sync(0xFFFFFFFFu, incl - t, l);
+                    break;
+                }
+                base += __shfl_sync(0xFFFFFFFFu, incl, 31);
+            }
+            if (lane == 0) {
+                tile_info[0] = seg;
+                if (seg >= 0) {
+                    const int r0 = a.starts[seg] + tile * NTOK, r1 = a.starts[seg + 1];
+                    tile_info[1] = r0;
+                    tile_info[2] = r1 - r0 < NTOK ? r1 - r0 : NTOK;
+                    tile_info[3] = a.experts[seg] * a.N;
+                }
+            }
+        }
+        __syncthreads();
+        if (tile_info[0] < 0) return;  // past the last tile (the whole cluster shares blockIdx.z)
+        tok0 = tile_info[1];
+        mt = tile_info[2];
+        wrow = tile_info[3];
+        __syncthreads();  // the shared words are overwritten by the rings below
+    }
     const int pairs = a.G >> 1;
     const int pb = rank * pairs / a.ks, pe = (rank + 1) * pairs / a.ks;
     const int g_begin = 2 * pb, GC = 2 * (pe - pb);  // this CTA's groups
@@ -254,9 +312,10 @@ __global__ void __launch_bounds__(TCV_THREADS, 1)
             if (lane == 0) {
                 mbar_arrive_expect_tx(&w_full[s], NMAT * S::WSLOT);
                 const int kx = (g_begin + wi * S::WG) * S::GW;
-                tma_load_2d(wring + (s * NMAT) * S::WSLOT, &tm_w0, &w_full[s], kx, a.row_off[0] + n0, pol);
+                tma_load_2d(wring + (s * NMAT) * S::WSLOT, &tm_w0, &w_full[s], kx, a.row_off[0] + wrow + n0, pol);
                 if (NMAT == 2)
-                    tma_load_2d(wring + (s * NMAT + 1) * S::WSLOT, &tm_w1, &w_full[s], kx, a.row_off[1] + n0, pol);
+                    tma_load_2d(wring + (s * NMAT + 1) * S::WSLOT, &tm_w1, &w_full[s], kx, a.row_off[1] + wrow + n0,
+                                pol);
             }
             __syncwarp();
         }
@@ -319,7 +378,7 @@ __global__ void __launch_bounds__(TCV_THREADS, 1)
             const int npairs = GC >> 1;
 #pragma unroll
             for (int m = 0; m < NMAT; ++m) {
-                const int grow = a.row_off[m] + n0 + r;
+                const int grow = a.row_off[m] + wrow + n0 + r;
                 const bool ok = grow < a.rows_total[m];
                 const size_t off = ok ? (size_t(grow) * a.G + g_begin) * 2 : 0;
                 const char* sg = reinterpret_cast<const char*>(a.sptr[m]) + off;
@@ -439,7 +498,7 @@ __global__ void __launch_bounds__(TCV_THREADS, 1)
 // ------------------------------------------------------------------------------------------------
 
 template <typename T, int BITS, int NMAT, int NTOK>
-static int tcv_launch_t(const void* x, int x_rows, const QmvMats& mats, TcvArgs a, int ks, int ws_req,
+static int tcv_launch_t(const void* x, int x_rows, const QmvMats& mats, TcvArgs a, int ks, int ws_req, int gz,
                         cudaStream_t st) {
     using S = TcvShape<BITS, NMAT, NTOK>;
     const DeviceInfo& di = device_info();
@@ -452,7 +511,7 @@ static int tcv_launch_t(const void* x, int x_rows, const QmvMats& mats, TcvArgs 
     a.sbw = (gc_max / 2) | 1;
     const size_t sb_bytes = size_t(NMAT) * 2 * 128 * a.sbw * 4;
     const size_t bar_bytes = (4 * TCV_MAX_SLOTS + 2 * S::AS + 1) * 8 + 16;
-    const size_t budget = NTOK <= 64 ? di.smem_per_sm / 2 - 2048 : di.smem_optin - 1024;
+    size_t budget = NTOK <= 64 ? di.smem_per_sm / 2 - 2048 : di.smem_optin - 1024;
     const int nw_max = (gc_max + S::WG - 1) / S::WG;
     int ws = nw_max < TCV_MAX_SLOTS ? nw_max : TCV_MAX_SLOTS;
     int xs = gc_max < TCV_MAX_SLOTS ? gc_max : TCV_MAX_SLOTS;
@@ -466,6 +525,8 @@ static int tcv_launch_t(const void* x, int x_rows, const QmvMats& mats, TcvArgs 
         return wb;
     };
     auto total = [&](int w, int x) { return ring_bytes(w, x) + size_t(x) * S::XSLOT + sb_bytes + bar_bytes + 1024; };
+    // half an SM when the rings fit (the next launch's CTAs can then start beside this one), else all of it
+    if (total(2, 2) > budget) budget = di.smem_optin - 1024;
     // weights first (their loads run ahead of the dependency), then x
     while (total(ws, xs) > budget && xs > 4) --xs;
     while (total(ws, xs) > budget && ws > 2) --ws;
@@ -509,7 +570,7 @@ static int tcv_launch_t(const void* x, int x_rows, const QmvMats& mats, TcvArgs 
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return LQ_E_CUDA;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((a.N + 127) / 128, ks, (a.M + NTOK - 1) / NTOK);
+    cfg.gridDim = dim3((a.N + 127) / 128, ks, gz > 0 ? gz : (a.M + NTOK - 1) / NTOK);
     cfg.blockDim = dim3(TCV_THREADS, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
@@ -533,15 +594,32 @@ static int tcv_launch_t(const void* x, int x_rows, const QmvMats& mats, TcvArgs 
 
 template <typename T, int BITS, int NMAT>
 static int tcv_dispatch_tok(int ntok, const void* x, int x_rows, const QmvMats& mats, const TcvArgs& a, int ks, int ws,
-                            cudaStream_t st) {
-    if (ntok == 16) return tcv_launch_t<T, BITS, NMAT, 16>(x, x_rows, mats, a, ks, ws, st);
-    if (ntok == 32) return tcv_launch_t<T, BITS, NMAT, 32>(x, x_rows, mats, a, ks, ws, st);
-    if (ntok == 64) return tcv_launch_t<T, BITS, NMAT, 64>(x, x_rows, mats, a, ks, ws, st);
-    if (ntok == 128) return tcv_launch_t<T, BITS, NMAT, 128>(x, x_rows, mats, a, ks, ws, st);
+                            int gz, cudaStream_t st) {
+    if (ntok == 16) return tcv_launch_t<T, BITS, NMAT, 16>(x, x_rows, mats, a, ks, ws, gz, st);
+    if (ntok == 32) return tcv_launch_t<T, BITS, NMAT, 32>(x, x_rows, mats, a, ks, ws, gz, st);
+    if (ntok == 64) return tcv_launch_t<T, BITS, NMAT, 64>(x, x_rows, mats, a, ks, ws, gz, st);
+    if (ntok == 128) return tcv_launch_t<T, BITS, NMAT, 128>(x, x_rows, mats, a, ks, ws, gz, st);
     if constexpr (NMAT == 1) {
-        if (ntok == 256) return tcv_launch_t<T, BITS, NMAT, 256>(x, x_rows, mats, a, ks, ws, st);
+        if (ntok == 256) return tcv_launch_t<T, BITS, NMAT, 256>(x, x_rows, mats, a, ks, ws, gz, st);
     }
     return LQ_E_UNSUPPORTED;
+}
+
+static int tcv_dispatch(const void* x, int x_rows, const QmvMats& mats, int nmat, const TcvArgs& a, int bits, int dtype,
+                        int ntok, int ks, int ws, int gz, cudaStream_t st) {
+    const bool bf16 = dtype == LQ_BF16;
+    if (bits == 4) {
+        if (nmat == 1)
+            return bf16 ? tcv_dispatch_tok<__nv_bfloat16, 4, 1>(ntok, x, x_rows, mats, a, ks, ws, gz, st)
+                        : tcv_dispatch_tok<__half, 4, 1>(ntok, x, x_rows, mats, a, ks, ws, gz, st);
+        return bf16 ? tcv_dispatch_tok<__nv_bfloat16, 4, 2>(ntok, x, x_rows, mats, a, ks, ws, gz, st)
+                    : tcv_dispatch_tok<__half, 4, 2>(ntok, x, x_rows, mats, a, ks, ws, gz, st);
+    }
+    if (nmat == 1)
+        return bf16 ? tcv_dispatch_tok<__nv_bfloat16, 8, 1>(ntok, x, x_rows, mats, a, ks, ws, gz, st)
+                    : tcv_dispatch_tok<__half, 8, 1>(ntok, x, x_rows, mats, a, ks, ws, gz, st);
+    return bf16 ? tcv_dispatch_tok<__nv_bfloat16, 8, 2>(ntok, x, x_rows, mats, a, ks, ws, gz, st)
+                : tcv_dispatch_tok<__half, 8, 2>(ntok, x, x_rows, mats, a, ks, ws, gz, st);
 }
 
 // K slices for rb row tiles: about 1.3 CTAs per SM in total (measured on B200 over the fused QKV,
@@ -581,19 +659,37 @@ int tcv_run(const void* x, int M, const QmvMats& mats, int nmat, int N, int K, i
     if (ntok == 0) ntok = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 || nmat == 2 ? 128 : 256;
     if (ntok != 16 && ntok != 32 && ntok != 64 && ntok != 128 && ntok != 256) return LQ_E_ARG;
     if (ks == 0) ks = tcv_default_ks((N + 127) / 128 * ((M + ntok - 1) / ntok), a.G / 2, device_info().sm_count);
-    const bool bf16 = dtype == LQ_BF16;
-    if (bits == 4) {
-        if (nmat == 1)
-            return bf16 ? tcv_dispatch_tok<__nv_bfloat16, 4, 1>(ntok, x, M, mats, a, ks, ws, st)
-                        : tcv_dispatch_tok<__half, 4, 1>(ntok, x, M, mats, a, ks, ws, st);
-        return bf16 ? tcv_dispatch_tok<__nv_bfloat16, 4, 2>(ntok, x, M, mats, a, ks, ws, st)
-                    : tcv_dispatch_tok<__half, 4, 2>(ntok, x, M, mats, a, ks, ws, st);
-    }
-    if (nmat == 1)
-        return bf16 ? tcv_dispatch_tok<__nv_bfloat16, 8, 1>(ntok, x, M, mats, a, ks, ws, st)
-                    : tcv_dispatch_tok<__half, 8, 1>(ntok, x, M, mats, a, ks, ws, st);
-    return bf16 ? tcv_dispatch_tok<__nv_bfloat16, 8, 2>(ntok, x, M, mats, a, ks, ws, st)
-                : tcv_dispatch_tok<__half, 8, 2>(ntok, x, M, mats, a, ks, ws, st);
+    return tcv_dispatch(x, M, mats, nmat, a, bits, dtype, ntok, ks, ws, 0, st);
+}
+
+// Grouped expert GEMMs (the MoE path): x = the expert-sorted rows xs (P rows), weights stacked (E, N, ...).
+// Token tiles of 16/32/64 rows from the expected rows per expert; one K slice (the grid is large).
+int tcv_run_grouped(const void* xs, int P, const QmvMats& mats, int nmat, int N, int K, void* out,
+                    const int32_t* starts, const int32_t* experts, const int32_t* nseg, int E, int bits, int dtype,
+                    const int* p, cudaStream_t st) {
+    if (!tcv_shape_ok(P, K, bits)) return LQ_E_SHAPE;
+    TcvArgs a = {};
+    a.M = P;
+    a.N = N;
+    a.K = K;
+    a.G = K / 64;
+    a.nseg_out = 1;
+    a.out[0] = out;
+    a.seg_end[0] = N;
+    a.ldo[0] = N;
+    a.grouped = 1;
+    a.starts = starts;
+    a.experts = experts;
+    a.nseg = nseg;
+    a.n_experts = E;
+    const int used = E < P ? E : P;
+    const int expect = (P + used - 1) / used;
+    int ntok = p ? p[0] : 0;
+    if (ntok == 0) ntok = expect >= 24 ? 64 : expect >= 12 ? 32 : 16;
+    if (ntok != 16 && ntok != 32 && ntok != 64) return LQ_E_ARG;
+    // tiles: at most one partial tile per used expert plus P / ntok full ones
+    const int gz = used + (P + ntok - 1) / ntok;
+    return tcv_dispatch(xs, P, mats, nmat, a, bits, dtype, ntok, 1, p ? p[2] : 0, gz, st);
 }
 
 }  // namespace lq

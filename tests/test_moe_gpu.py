@@ -63,7 +63,7 @@ def test_route_topk_nan(cuda):
         assert len(set(row.tolist())) == 4 and row.max() < 64 and 3 not in row.tolist()
 
 
-@pytest.mark.parametrize("P,E", [(4, 64), (2048, 64), (37, 8), (300, 512)])
+@pytest.mark.parametrize("P,E", [(4, 64), (2048, 64), (37, 8), (300, 512), (20000, 64), (9000, 1024)])
 def test_group(cuda, P, E):
     import torch
     from locals_b200 import moe
