@@ -225,12 +225,16 @@ __device__ __forceinline__ void qmv_iteration(float (&acc)[NMAT][MT][4], uint32_
     }
 }
 
-template <typename T, int BITS, int MT, int WK, int NMAT>
+// DENSE: one token segment, no gather, no cluster -- the decode case, compiled without the grouped, gather and
+// split-K paths so the hot loop's code stays small (instruction-cache misses were the top stall).
+template <typename T, int BITS, int MT, int WK, int NMAT, bool DENSE>
 __global__ void __launch_bounds__(QMV_THREADS, (MT * NMAT <= 2) ? 2 : 1)
     qmv_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
                const __grid_constant__ CUtensorMap tm_x, const QmvArgs a) {
     using S = QmvShape<T, BITS, MT, WK, NMAT>;
     constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+    const bool grouped = !DENSE && a.grouped;
+    const int kslices = DENSE ? 1 : a.ks;
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -242,14 +246,14 @@ __global__ void __launch_bounds__(QMV_THREADS, (MT * NMAT <= 2) ? 2 : 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * S::BN;
-    const int krank = (a.ks > 1) ? int(cluster_ctarank()) : 0;
+    const int krank = (kslices > 1) ? int(cluster_ctarank()) : 0;
     const int c_begin = (a.nchunk * krank) / a.ks;
     const int c_end = (a.nchunk * (krank + 1)) / a.ks;
     const int nloc = c_end - c_begin;
 
     // segment: dense calls have one, rows [0, M), weights at row 0
     int seg_row0 = 0, seg_rows = a.M, wrow0 = 0;
-    if (a.grouped) {
+    if (grouped) {
         grid_dep_wait();  // starts / experts / nseg come from the grouping kernel
         const int sgi = blockIdx.z;
         if (sgi >= a.nseg[0]) return;  // the whole cluster shares blockIdx.z: it exits together
@@ -264,7 +268,7 @@ __global__ void __launch_bounds__(QMV_THREADS, (MT * NMAT <= 2) ? 2 : 1)
         wrow0 = e * a.N;
     }
     int ntb = (seg_rows + S::MTOK - 1) / S::MTOK;
-    if (a.ks > 1 && ntb > 1) ntb = 1;  // (the host never launches split-K with longer segments)
+    if (kslices > 1 && ntb > 1) ntb = 1;  // (the host never launches split-K with longer segments)
     const int total = ntb * nloc;
 
     if (threadIdx.x == 0) {
@@ -301,7 +305,7 @@ __global__ void __launch_bounds__(QMV_THREADS, (MT * NMAT <= 2) ? 2 : 1)
         const int kg = a.K / 64;  // groups per row
         const int vb = a.sb_vec;  // bytes per cp.async
         const int units_row = S::SBROW / vb;
-        const bool gather = a.gather != nullptr;
+        const bool gather = !DENSE && a.gather != nullptr;
         // weights (TMA, lane 0) and scales/biases (cp.async, all lanes) of local chunk i into stage s
         auto load_weights = [&](int i, int s) {
             const uint32_t st = smem_base + s * S::STAGE_BYTES;
@@ -366,7 +370,7 @@ __global__ void __launch_bounds__(QMV_THREADS, (MT * NMAT <= 2) ? 2 : 1)
             }
         };
         const int pre = total < ns ? total : ns;
-        if (!a.grouped) {
+        if (!grouped) {
             for (int i = 0; i < pre; ++i) {
                 load_weights(i, i);
                 cp_async_arrive(&full[i]);
@@ -393,7 +397,7 @@ __global__ void __launch_bounds__(QMV_THREADS, (MT * NMAT <= 2) ? 2 : 1)
     } else {
         // ------------------------------ consumer warps ------------------------------
         const uint32_t smem_base = smem_u32(smem);
-        if (!a.grouped) grid_dep_wait();  // (before any output store of this kernel)
+        if (!grouped) grid_dep_wait();  // (before any output store of this kernel)
         for (int i = 0; i < total; ++i) {
             const int s = i % ns;
             if (ok) ok = mbar_wait(&full[s], (i / ns) & 1);
@@ -435,7 +439,7 @@ __global__ void __launch_bounds__(QMV_THREADS, (MT * NMAT <= 2) ? 2 : 1)
                     }
                     named_barrier(1, 32 * QMV_CW);
                 }
-                if (a.ks == 1 && kq == 0 && ok) {
+                if (kslices == 1 && kq == 0 && ok) {
                     const int tb = i / nloc;
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
@@ -454,7 +458,7 @@ __global__ void __launch_bounds__(QMV_THREADS, (MT * NMAT <= 2) ? 2 : 1)
                         }
                     }
                 }
-                if (a.ks == 1) {
+                if (kslices == 1) {
 #pragma unroll
                     for (int m = 0; m < NMAT; ++m)
 #pragma unroll
@@ -465,7 +469,7 @@ __global__ void __launch_bounds__(QMV_THREADS, (MT * NMAT <= 2) ? 2 : 1)
             }
         }
     }
-    if (a.ks == 1) return;
+    if (kslices == 1) return;
 
     // ------------------ split-K over the cluster (one token block) ------------------
     if (warp < QMV_CW && kq == 0) {
@@ -479,7 +483,7 @@ __global__ void __launch_bounds__(QMV_THREADS, (MT * NMAT <= 2) ? 2 : 1)
                     part[(m * S::MTOK + tok) * S::BN + row] = ok ? acc[m][mt][e] : 0.0f;
                 }
     }
-    if (warp == QMV_CW && !a.grouped) grid_dep_wait();
+    if (warp == QMV_CW && !grouped) grid_dep_wait();
     cluster_sync();
     const uint32_t part_local = smem_u32(part);
     uint32_t peer[16];
@@ -572,7 +576,8 @@ static int qmv_launch_t(const void* x, int x_rows, const QmvMats& mats, QmvArgs 
     a.sb_vec = (S::SBROW == 16 && kg % 8 == 0) ? 16 : (kg % 4 == 0) ? 8 : 4;
     a.x = x;
 
-    auto kern = qmv_kernel<T, BITS, MT, WK, NMAT>;
+    const bool dense = !a.grouped && a.gather == nullptr && ks == 1;
+    auto kern = dense ? qmv_kernel<T, BITS, MT, WK, NMAT, true> : qmv_kernel<T, BITS, MT, WK, NMAT, false>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return LQ_E_CUDA;
     if (ks > 8) {
