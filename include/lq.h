@@ -126,6 +126,16 @@ int lq_moe_experts(const void* xs, const int32_t* starts, const int32_t* experts
 int lq_moe_combine(const void* ys, const float* weights, const int32_t* pos, void* y, int T, int k, int D, int dtype,
                    void* stream);
 
+/* 1 if kernel family `family` (LQ_FAM_*; LQ_FAM_AUTO = any) accepts this shape and format, else 0. Host-only,
+ * needs no GPU. Replaces the per-family supported(M, K, N, cfg) predicates the reference's tuner filters
+ * its candidates with (locals/qmv_frag.py:162,519; locals/nax_kernel.py:399-408; locals/kernels.py:654-674). */
+int lq_supported(int family, int M, int N, int K, int bits, int group_size, int dtype);
+
+/* The tuning candidates for one shape (the reference's candidate list, locals/kernels.py:654-674): writes
+ * up to max_cfgs entries (family + parameters, 0 = the library's choice) into cfgs and returns how many
+ * exist (cfgs may be NULL to count). Host-only, needs no GPU. */
+int lq_list_configs(int M, int N, int K, int bits, int group_size, int dtype, lq_cfg* cfgs, int max_cfgs);
+
 /* Read (and with clear != 0 reset) the device status word kernels OR their LQ_DEV_* codes into
  * (1 = a bounded wait gave up, 2 = an index check failed, 4 = a TMEM allocation failed). Synchronizes
  * the current device. Returns the word, or 0xffffffff if the read itself failed. */

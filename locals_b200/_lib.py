@@ -37,6 +37,8 @@ SIGNATURES = {
                         _vp, _i, _vp], _i),
     "lq_moe_route": ([_vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp], _i),
     "lq_moe_combine": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp], _i),
+    "lq_supported": ([_i, _i, _i, _i, _i, _i, _i], _i),
+    "lq_list_configs": ([_i, _i, _i, _i, _i, _i, ctypes.POINTER(Cfg), _i], _i),
     "lq_device_status": ([_i], ctypes.c_uint),
     "lq_last_cuda_error": ([], ctypes.c_char_p),
     "lq_strerror": ([_i], ctypes.c_char_p),

@@ -317,6 +317,64 @@ int lq_moe_experts(const void* xs, const int32_t* starts, const int32_t* experts
                           reinterpret_cast<cudaStream_t>(stream)));
 }
 
+int lq_supported(int family, int M, int N, int K, int bits, int group_size, int dtype) {
+    if (!is16(dtype) || (bits != 4 && bits != 8) || group_size != 64) return 0;
+    if (M < 1 || N < 1 || K < 64 || K % 64) return 0;
+    const bool qmv = qmv_shape_ok(K, bits), tcv = tcv_shape_ok(M, K, bits), tc = tc_shape_ok(M, N, K, bits);
+    switch (family) {
+        case LQ_FAM_AUTO: return (qmv || tcv || (M > 64 && tc)) ? 1 : 0;
+        case LQ_FAM_QMV: return qmv ? 1 : 0;
+        case LQ_FAM_TCV: return tcv ? 1 : 0;
+        case LQ_FAM_TC: return tc ? 1 : 0;
+        default: return 0;
+    }
+}
+
+int lq_list_configs(int M, int N, int K, int bits, int group_size, int dtype, lq_cfg* cfgs, int max_cfgs) {
+    int n = 0;
+    auto add = [&](int fam, int p0, int p1, int p2, int p3) {
+        if (cfgs && n < max_cfgs) {
+            lq_cfg c = {};
+            c.family = fam;
+            c.p[0] = p0;
+            c.p[1] = p1;
+            c.p[2] = p2;
+            c.p[3] = p3;
+            cfgs[n] = c;
+        }
+        ++n;
+    };
+    if (!lq_supported(LQ_FAM_AUTO, M, N, K, bits, group_size, dtype)) return 0;
+    if (lq_supported(LQ_FAM_QMV, M, N, K, bits, group_size, dtype)) {
+        add(LQ_FAM_QMV, 0, 0, 0, 0);
+        if (M <= 64) {
+            const int bk = 2048 / bits;
+            const int nchunk = (K + bk - 1) / bk;
+            const int mt = M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8;
+            const int wks[3] = {1, 2, 4}, kss[6] = {1, 2, 3, 4, 5, 8};
+            for (int wk : wks) {
+                if (mt >= 4 && wk > 2) continue;
+                for (int ks : kss)
+                    if (ks <= nchunk) add(LQ_FAM_QMV, mt, wk, ks, 0);
+            }
+        }
+    }
+    if (lq_supported(LQ_FAM_TCV, M, N, K, bits, group_size, dtype)) {
+        add(LQ_FAM_TCV, 0, 0, 0, 0);
+        const int kss[6] = {1, 2, 3, 4, 6, 8};
+        for (int ks : kss)
+            if (ks <= K / 128) add(LQ_FAM_TCV, 0, ks, 0, 0);
+        if (M > 64) add(LQ_FAM_TCV, M > 128 ? 256 : 128, 1, 0, 0);
+    }
+    if (M > 64 && lq_supported(LQ_FAM_TC, M, N, K, bits, group_size, dtype)) {
+        add(LQ_FAM_TC, 0, 0, 0, 0);
+        const int bns[3] = {256, 224, 128};
+        for (int bn : bns)
+            if (N % bn == 0) add(LQ_FAM_TC, bn, 0, 0, 0);
+    }
+    return n;
+}
+
 int lq_moe_combine(const void* ys, const float* weights, const int32_t* pos, void* y, int T, int k, int D, int dtype,
                    void* stream) {
     if (!ys || !weights || !y) return LQ_E_ARG;

@@ -176,29 +176,29 @@ def launch(choice: Sequence, M: int, K: int, N: int, dtype: torch.dtype, bits: i
     return f
 
 
-def candidates(M: int, K: int, N: int, bits: int = 4) -> list:
-    """Tuning candidates for one shape (the analogue of locals/kernels.py:654-674): decode tilings
-    ("qmv", MT token tiles of 8, WK warps splitting K per 16-row fragment, KS cluster split-K, NS stages,
-    0 = the library's choice) and, from PREFILL_M rows, the tensor-core GEMM."""
-    out = [("qmv", 0, 0, 0, 0)]
-    if M <= MAX_SMALL_M:
-        bk = 2048 // bits
-        nchunk = max(1, (K + bk - 1) // bk)
-        mt0 = 1 if M <= 8 else 2 if M <= 16 else 4 if M <= 32 else 8
-        for wk in (1, 2, 4):
-            if mt0 >= 4 and wk > 2:
-                continue
-            for ks in (1, 2, 3, 4, 5, 8):
-                if ks <= nchunk:
-                    out.append(("qmv", mt0, wk, ks, 0))
-        if K % 128 == 0:
-            out.append(("tcv", 0, 0, 0))
-            for ks in (1, 2, 3, 4, 6, 8):
-                if ks <= K // 128:
-                    out.append(("tcv", 0, ks, 0))
-    if M >= PREFILL_M:
-        out.append(("tc",))
+_FAMILY_NAME = {v: k for k, v in _FAMILY.items()}
+_NPARAM = {"qmv": 4, "tcv": 3, "tc": 1}
+
+
+def candidates(M: int, K: int, N: int, bits: int = 4, dtype: torch.dtype = torch.bfloat16) -> list:
+    """Tuning candidates for one shape (the analogue of locals/kernels.py:654-674), from the library's own
+    list (``lq_list_configs``): decode tilings ("qmv", MT token tiles of 8, WK warps splitting K per
+    16-row fragment, KS cluster split-K, NS stages), ("tcv", NTOK token tile, KS split-K, WS weight slots)
+    and, from 65 rows, ("tc", BN); 0 = the library's choice."""
+    L = _lib.lib()
+    n = L.lq_list_configs(M, N, K, bits, 64, dtype_code(dtype), None, 0)
+    arr = (_lib.Cfg * max(n, 1))()
+    L.lq_list_configs(M, N, K, bits, 64, dtype_code(dtype), arr, n)
+    out = []
+    for c in arr[:n]:
+        name = _FAMILY_NAME[c.family]
+        out.append((name,) + tuple(int(v) for v in c.p[: _NPARAM[name]]))
     return out
+
+
+def supported(family: str, M: int, K: int, N: int, bits: int = 4, dtype: torch.dtype = torch.bfloat16) -> bool:
+    """Whether a kernel family takes this shape (``lq_supported``)."""
+    return bool(_lib.lib().lq_supported(_FAMILY[family], M, N, K, bits, 64, dtype_code(dtype)))
 
 
 # ---- a quantized linear layer ----------------------------------------------------------------------

@@ -100,7 +100,7 @@ def choose(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch
     ncopy = max(1, min(32, l2_bytes // max(nbytes, 1)))
     copies = [(w.clone(), scales.clone(), biases.clone()) for _ in range(ncopy)]
     best, best_t = None, float("inf")
-    for c in kernels.candidates(M, K, N, bits):
+    for c in kernels.candidates(M, K, N, bits, x.dtype):
         try:
             got = kernels.quantized_matmul(x, w, scales, biases, group_size=group_size, bits=bits, choice=c).float()
         except kernels._lib.LQError:

@@ -74,3 +74,29 @@ def test_routing_args_rejected():
     assert L.lq_route_topk(fake, 4, 64, 4, 2, fake, fake, None) == _lib.LQ_E_ARG
     assert L.lq_route_topk(fake, 4, 2048, 4, 0, fake, fake, None) == _lib.LQ_E_SHAPE
     assert L.lq_moe_group(None, 4, 64, fake, fake, fake, fake, None, None) == _lib.LQ_E_ARG
+
+
+def test_supported_and_candidates():
+    # host-only: the family predicates and the tuner's candidate list, no GPU needed
+    from locals_b200 import kernels
+    from locals_b200._lib import lib
+
+    L = lib()
+    # (family, M, N, K, bits, group, dtype) -> expected
+    assert L.lq_supported(1, 16, 6144, 2560, 4, 64, 1) == 1   # qmv: 4-bit K % 256 == 0
+    assert L.lq_supported(1, 16, 6144, 2496, 4, 64, 1) == 0   # 4-bit K not a multiple of 256
+    assert L.lq_supported(3, 16, 6144, 2560, 4, 64, 1) == 1   # tcv: K % 128 == 0
+    assert L.lq_supported(3, 16, 6144, 2496, 4, 64, 1) == 0
+    assert L.lq_supported(2, 2048, 14336, 4096, 4, 64, 1) == 1  # tc
+    assert L.lq_supported(0, 16, 6144, 2560, 4, 32, 1) == 0   # group 32 is not built
+    assert L.lq_supported(0, 16, 6144, 2560, 3, 64, 1) == 0   # 3-bit is not built
+    assert L.lq_supported(0, 16, 6144, 2560, 4, 64, 2) == 0   # fp32 activations are not built
+    assert L.lq_supported(7, 16, 6144, 2560, 4, 64, 1) == 0   # unknown family
+    dec = kernels.candidates(16, 2560, 6144, 4)
+    assert dec[0] == ("qmv", 0, 0, 0, 0) and ("tcv", 0, 0, 0) in dec
+    assert all(c[0] in ("qmv", "tcv") for c in dec)
+    pre = kernels.candidates(2048, 4096, 14336, 4)
+    assert ("tc", 0) in pre and ("tc", 256) in pre and ("tcv", 256, 1, 0) in pre
+    assert L.lq_list_configs(16, 6144, 2560, 4, 64, 1, None, 0) == len(dec)
+    assert kernels.candidates(16, 2496, 6144, 4) == [] or all(c[0] != "tcv" for c in kernels.candidates(16, 2496, 6144, 4))
+    assert kernels.supported("tc", 2048, 4096, 14336) and not kernels.supported("qmv", 16, 2496, 6144)
