@@ -36,7 +36,8 @@ extern "C" {
 #define LQ_FAM_AUTO 0   /* pick by shape: TC from 65 rows; TCV for 33-64 rows or >= 24 MB of weights from 9 rows; else QMV */
 #define LQ_FAM_QMV 1    /* decode: TMA-staged packed weights, register dequant, mma.sync; p = {MT, WK, KS, NS} */
 #define LQ_FAM_TC 2     /* prefill: dequant tiles into shared memory, tcgen05.mma into TMEM */
-#define LQ_FAM_TCV 3    /* decode on tcgen05: dequant into TMEM (A operand), tokens as N; p = {NTOK, KS, WS} */
+#define LQ_FAM_TCV 3    /* tcgen05 with weights dequantized into TMEM (A operand), tokens as N;
+                           p = {NTOK, KS, WS, PERSISTENT (1: one CTA per SM walks the tiles)} */
 
 typedef struct lq_cfg {
     int family;  /* LQ_FAM_* */

@@ -36,6 +36,12 @@ int tcv_run(const void* x, int M, const QmvMats& mats, int nmat, int N, int K, i
 int tcv_run_grouped(const void* xs, int P, const QmvMats& mats, int nmat, int N, int K, void* out,
                     const int32_t* starts, const int32_t* experts, const int32_t* nseg, int E, int bits, int dtype,
                     const int* p, cudaStream_t st);
+bool tcvp_shape_ok(int M, int K, int bits);
+int tcvp_run(const void* x, int M, const QmvMats& mats, int nmat, int N, int K, int nout, void* const* outs,
+             const int* seg_end, const int* ldo, int bits, int dtype, int ntok, cudaStream_t st);
+int tcvp_run_grouped(const void* xs, int P, const QmvMats& mats, int nmat, int N, int K, void* out,
+                     const int32_t* starts, const int32_t* experts, const int32_t* nseg, int E, int bits, int dtype,
+                     int ntok, cudaStream_t st);
 }  // namespace lq
 
 using namespace lq;
@@ -108,6 +114,10 @@ static int qmm_common(const void* x, const uint32_t* w, const void* s, const voi
     }
     const QmvMats mats = one_matrix(w, s, b, N);
     if (fam == LQ_FAM_TCV) {
+        if (cfg->p[3] == 1) {  // persistent form
+            if (!tcvp_shape_ok(M, K, bits)) return LQ_E_SHAPE;
+            return finish(tcvp_run(x, M, mats, 1, N, K, nout, outs, a.seg_end, a.ldo, bits, dtype, cfg->p[0], st));
+        }
         if (!tcv_shape_ok(M, K, bits)) return LQ_E_SHAPE;
         return finish(tcv_run(x, M, mats, 1, N, K, nout, outs, a.seg_end, a.ldo, bits, dtype, cfg->p, st));
     }
@@ -180,6 +190,11 @@ int lq_qmm_glu(const void* x, const uint32_t* w_gate, const void* s_gate, const 
     const int fam = cfg ? cfg->family : LQ_FAM_AUTO;
     void* outs[1] = {h};
     if (fam == LQ_FAM_TCV) {
+        if (cfg->p[3] == 1) {
+            if (!tcvp_shape_ok(M, K, bits)) return LQ_E_SHAPE;
+            return finish(tcvp_run(x, M, m, 2, I, K, 1, outs, a.seg_end, a.ldo, bits, dtype, cfg->p[0],
+                                   reinterpret_cast<cudaStream_t>(stream)));
+        }
         if (!tcv_shape_ok(M, K, bits)) return LQ_E_SHAPE;
         return finish(tcv_run(x, M, m, 2, I, K, 1, outs, a.seg_end, a.ldo, bits, dtype, cfg->p,
                               reinterpret_cast<cudaStream_t>(stream)));
@@ -304,11 +319,19 @@ int lq_moe_experts(const void* xs, const int32_t* starts, const int32_t* experts
     m.b[1] = glu ? b1 : b0;
     m.rows_total[0] = m.rows_total[1] = E * N;
     if (gather_order && gather_k < 1) return LQ_E_ARG;
-    // from 128 routed rows the expert GEMMs run on the tensor-core family (pre-gathered rows only)
-    if (!gather_order && P >= 128 && tcv_shape_ok(P, K, bits)) {
-        rc = tcv_run_grouped(xs, P, m, glu ? 2 : 1, N, K, out, starts, experts, nseg, E, bits, dtype, nullptr,
-                             reinterpret_cast<cudaStream_t>(stream));
-        if (rc != LQ_E_SHAPE) return finish(rc);
+    // from 1024 routed rows (about 16 per expert at 64 experts) the expert GEMMs run on the tensor-core
+    // family, persistent when K allows (pre-gathered rows only); below that the mma.sync family's grouped
+    // mode measured faster on B200
+    if (!gather_order && P >= 1024) {
+        const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+        if (tcvp_shape_ok(P, K, bits)) {  // persistent: one CTA per SM walks the expert tiles
+            rc = tcvp_run_grouped(xs, P, m, glu ? 2 : 1, N, K, out, starts, experts, nseg, E, bits, dtype, 0, st);
+            if (rc != LQ_E_SHAPE) return finish(rc);
+        }
+        if (tcv_shape_ok(P, K, bits)) {
+            rc = tcv_run_grouped(xs, P, m, glu ? 2 : 1, N, K, out, starts, experts, nseg, E, bits, dtype, nullptr, st);
+            if (rc != LQ_E_SHAPE) return finish(rc);
+        }
     }
     a.gather = gather_order;
     a.gather_k = gather_k;
@@ -365,6 +388,7 @@ int lq_list_configs(int M, int N, int K, int bits, int group_size, int dtype, lq
         for (int ks : kss)
             if (ks <= K / 128) add(LQ_FAM_TCV, 0, ks, 0, 0);
         if (M > 64) add(LQ_FAM_TCV, M > 128 ? 256 : 128, 1, 0, 0);
+        if (tcvp_shape_ok(M, K, bits)) add(LQ_FAM_TCV, 0, 0, 0, 1);  // the persistent form
     }
     if (M > 64 && lq_supported(LQ_FAM_TC, M, N, K, bits, group_size, dtype)) {
         add(LQ_FAM_TC, 0, 0, 0, 0);

@@ -4,6 +4,7 @@
 #include "quant.cu"
 #include "qmv.cu"
 #include "tcv.cu"
+#include "tcvp.cu"
 #include "moe.cu"
 #include "tc_gemm.cu"
 #include "capi.cu"

@@ -127,8 +127,10 @@ template <int N>
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]) {
     if constexpr (N == 8)
         tmem_ld_32x32b_x8(taddr, r);
-    else
+    else if constexpr (N == 16)
         tmem_ld_32x32b_x16(taddr, r);
+    else
+        tmem_ld_32x32b_x32(taddr, r);
 }
 
 // One weight row of one 64-wide group -> 32 packed pairs (k = 2j, 2j+1) in the activation dtype. The

@@ -11,8 +11,9 @@ every path is a hand-written sm_100a kernel of liblq.so:
 
 * ``("qmv", MT, WK, KS, NS)`` -- decode family (TMA-staged packed weights, register dequant into
   mma.sync fragments, cluster split-K), any M (weights streamed once per 64 rows);
-* ``("tcv", NTOK, KS, WS)`` -- decode on the tensor cores (weights dequantized into tensor memory as
-  the MMA's A operand, tokens as its N side, 16/32/64 columns), M <= 64, K % 128 == 0;
+* ``("tcv", NTOK, KS, WS[, PERSISTENT])`` -- the tensor-core family with weights dequantized into tensor
+  memory as the MMA's A operand and tokens as its N side (16..256 columns); PERSISTENT = 1 runs one CTA
+  per SM over all tiles (K % 256 == 0 at 4 bits);
 * ``("tc", ...)`` -- prefill family (dequantized tiles in shared memory feeding tcgen05.mma with
   TMEM accumulators), M >= 128.
 
@@ -177,14 +178,14 @@ def launch(choice: Sequence, M: int, K: int, N: int, dtype: torch.dtype, bits: i
 
 
 _FAMILY_NAME = {v: k for k, v in _FAMILY.items()}
-_NPARAM = {"qmv": 4, "tcv": 3, "tc": 1}
+_NPARAM = {"qmv": 4, "tcv": 4, "tc": 1}
 
 
 def candidates(M: int, K: int, N: int, bits: int = 4, dtype: torch.dtype = torch.bfloat16) -> list:
     """Tuning candidates for one shape (the analogue of locals/kernels.py:654-674), from the library's own
     list (``lq_list_configs``): decode tilings ("qmv", MT token tiles of 8, WK warps splitting K per
-    16-row fragment, KS cluster split-K, NS stages), ("tcv", NTOK token tile, KS split-K, WS weight slots)
-    and, from 65 rows, ("tc", BN); 0 = the library's choice."""
+    16-row fragment, KS cluster split-K, NS stages), ("tcv", NTOK token tile, KS split-K, WS weight slots,
+    PERSISTENT) and, from 65 rows, ("tc", BN); 0 = the library's choice."""
     L = _lib.lib()
     n = L.lq_list_configs(M, N, K, bits, 64, dtype_code(dtype), None, 0)
     arr = (_lib.Cfg * max(n, 1))()

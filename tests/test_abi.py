@@ -93,10 +93,10 @@ def test_supported_and_candidates():
     assert L.lq_supported(0, 16, 6144, 2560, 4, 64, 2) == 0   # fp32 activations are not built
     assert L.lq_supported(7, 16, 6144, 2560, 4, 64, 1) == 0   # unknown family
     dec = kernels.candidates(16, 2560, 6144, 4)
-    assert dec[0] == ("qmv", 0, 0, 0, 0) and ("tcv", 0, 0, 0) in dec
+    assert dec[0] == ("qmv", 0, 0, 0, 0) and ("tcv", 0, 0, 0, 0) in dec and ("tcv", 0, 0, 0, 1) in dec
     assert all(c[0] in ("qmv", "tcv") for c in dec)
     pre = kernels.candidates(2048, 4096, 14336, 4)
-    assert ("tc", 0) in pre and ("tc", 256) in pre and ("tcv", 256, 1, 0) in pre
+    assert ("tc", 0) in pre and ("tc", 256) in pre and ("tcv", 256, 1, 0, 0) in pre
     assert L.lq_list_configs(16, 6144, 2560, 4, 64, 1, None, 0) == len(dec)
     assert kernels.candidates(16, 2496, 6144, 4) == [] or all(c[0] != "tcv" for c in kernels.candidates(16, 2496, 6144, 4))
     assert kernels.supported("tc", 2048, 4096, 14336) and not kernels.supported("qmv", 16, 2496, 6144)

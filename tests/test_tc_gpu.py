@@ -50,7 +50,7 @@ def test_tc_tilings_agree(cuda, bn):
     assert rel_err(y.float().cpu().numpy(), ref) <= TOL_REL
 
 
-@pytest.mark.parametrize("choice", [("tc",), ("tcv", 256, 0, 0)])
+@pytest.mark.parametrize("choice", [("tc",), ("tcv", 256, 0, 0), ("tcv", 256, 0, 0, 1)])
 def test_tc_config5_full(cuda, choice):
     # both prefill formulations: x on the MMA's M side (tc), and weights dequantized into tensor memory
     # with 256-token tiles on N (tcv)

@@ -49,7 +49,7 @@ def test_tcv_configs(cuda, M, N, K, bits, dtype):
 @pytest.mark.parametrize("M,N,K,bits,dtype", [
     (3, 200, 512, 4, "float16"),
     (5, 136, 1024, 4, "bfloat16"),
-    (9, 72, 128, 4, "bfloat16"),
+    (9, 72, 256, 4, "bfloat16"),
     (17, 520, 768, 4, "float16"),
     (33, 96, 2048, 4, "bfloat16"),
     (64, 130, 512, 8, "float16"),
@@ -76,13 +76,45 @@ def test_tcv_every_tiling(cuda, choice):
     (100, 520, 768, 4, "bfloat16", 0),
     (300, 384, 1024, 4, "float16", 0),
     (130, 272, 512, 8, "bfloat16", 0),
-    (513, 256, 640, 4, "bfloat16", 256),
+    (513, 256, 768, 4, "bfloat16", 256),
     (200, 300, 1024, 8, "float16", 128),
     (70, 136, 2048, 4, "bfloat16", 16),
 ])
 def test_tcv_token_tiles(cuda, M, N, K, bits, dtype, ntok):
     y, ref = _run(cuda, M, N, K, bits, dtype, seed=M + N * 7 + K, choice=("tcv", ntok, 0, 0))
     assert rel_err(y, ref) <= TOL_REL
+
+
+# the persistent form (one CTA per SM walking the tiles): ragged tiles, both dtypes and bit widths
+@pytest.mark.parametrize("M,N,K,bits,dtype,ntok", [
+    (300, 384, 1024, 4, "float16", 0),
+    (513, 256, 768, 4, "bfloat16", 256),
+    (200, 300, 1024, 8, "float16", 128),
+    (70, 136, 2048, 4, "bfloat16", 16),
+    (64, 2560, 9728, 8, "bfloat16", 0),
+    (40, 1000, 512, 4, "bfloat16", 32),
+])
+def test_tcv_persistent(cuda, M, N, K, bits, dtype, ntok):
+    y, ref = _run(cuda, M, N, K, bits, dtype, seed=M * 3 + N + K, choice=("tcv", ntok, 0, 0, 1))
+    assert rel_err(y, ref) <= TOL_REL
+
+
+def test_tcv_persistent_glu(cuda):
+    import torch
+    from locals_b200 import kernels
+
+    rng = np.random.default_rng(31)
+    M, K, I = 150, 1024, 384
+    x = act(rng, M, K, "bfloat16")
+    gq, gs, gb = qweights(rng, I, K, 4, "bfloat16")
+    uq, us, ub = qweights(rng, I, K, 4, "bfloat16")
+    href = O.swiglu(O.round_to(O.qmm(x, gq, gs, gb, 64, 4), "bfloat16"),
+                    O.round_to(O.qmm(x, uq, us, ub, 64, 4), "bfloat16"), "bfloat16")
+    h = kernels.qmm_glu(x_torch(x, "bfloat16", cuda), to_torch(gq, gs, gb, "bfloat16", cuda),
+                        to_torch(uq, us, ub, "bfloat16", cuda), bits=4, choice=("tcv", 0, 0, 0, 1))
+    torch.cuda.synchronize()
+    assert rel_err(h.float().cpu().numpy(), href) <= 2.0 ** -6
+    assert kernels.device_status() == 0
 
 
 def test_tcv_split_and_glu(cuda):
