@@ -547,6 +547,7 @@ CASES = {
     "mlp64": "8-bit MLP gate||up + SiLU.mul and down at M=64, 4 layers",
     "tc": "prefill GEMM x bf16 [1024,4096] . 4-bit [7168,4096]^T",
     "moe16": "MoE layer, 64 experts top-4, D 2048, I 768, M=16",
+    "moe512": "MoE layer, 64 experts top-4, D 2048, I 768, M=512",
 }
 
 
@@ -580,7 +581,7 @@ def run_case(name):
         x = torch.randn((1024, 4096), generator=gen, device=dev).to(torch.bfloat16)
         for _ in range(4):
             kernels.quantized_matmul(x, w, s, b)
-    elif name == "moe16":
+    elif name in ("moe16", "moe512"):
         E, D, I = 64, 2048, 768
 
         def stack(N, Kd):
@@ -589,7 +590,7 @@ def run_case(name):
 
         layer = moe.MoELayer((torch.randn((E, D), generator=gen, device=dev) * 0.02).to(torch.float16),
                              stack(I, D), stack(I, D), stack(D, I), top_k=4)
-        x = torch.randn((16, D), generator=gen, device=dev).to(torch.bfloat16)
+        x = torch.randn((16 if name == "moe16" else 512, D), generator=gen, device=dev).to(torch.bfloat16)
         for _ in range(3):
             layer(x)
     else:

@@ -191,9 +191,8 @@ __device__ __forceinline__ void tcv_dequant_row(uint32_t rowp, int r, int c0, ui
 }
 
 template <typename T, int BITS, int NMAT, int NTOK>
-__global__ void __launch_bounds__(TCV_THREADS, 1)
-    tcv_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
-               const __grid_constant__ CUtensorMap tm_x, const TcvArgs a) {
+__device__ __forceinline__ void tcv_body(const CUtensorMap& tm_w0, const CUtensorMap& tm_w1, const CUtensorMap& tm_x,
+                                         const TcvArgs& a) {
     using S = TcvShape<BITS, NMAT, NTOK>;
     constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
 
@@ -497,6 +496,24 @@ __global__ void __launch_bounds__(TCV_THREADS, 1)
     }
 }
 
+// Decode tiles (up to 64 tokens) at 64 registers: the register file is split over the SM's four
+// sub-partitions and a 14-warp CTA puts four warps on some of them, so a second CTA -- the next launch's,
+// loading its weights while this one computes -- fits beside it only at <= 64 registers (one launch still
+// places one CTA per SM: the kernel holds tensor memory). Wide tiles (prefill) take what they need.
+template <typename T, int BITS, int NMAT, int NTOK>
+__global__ void __maxnreg__(64)
+    tcv_kernel_dec(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
+                   const __grid_constant__ CUtensorMap tm_x, const TcvArgs a) {
+    tcv_body<T, BITS, NMAT, NTOK>(tm_w0, tm_w1, tm_x, a);
+}
+
+template <typename T, int BITS, int NMAT, int NTOK>
+__global__ void __launch_bounds__(TCV_THREADS, 1)
+    tcv_kernel_wide(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
+                    const __grid_constant__ CUtensorMap tm_x, const TcvArgs a) {
+    tcv_body<T, BITS, NMAT, NTOK>(tm_w0, tm_w1, tm_x, a);
+}
+
 // ------------------------------------------------------------------------------------------------
 
 template <typename T, int BITS, int NMAT, int NTOK>
@@ -568,7 +585,11 @@ static int tcv_launch_t(const void* x, int x_rows, const QmvMats& mats, TcvArgs 
         if (rc) return rc;
     }
 
-    auto kern = tcv_kernel<T, BITS, NMAT, NTOK>;
+    void (*kern)(CUtensorMap, CUtensorMap, CUtensorMap, TcvArgs);
+    if constexpr (NTOK <= 64)
+        kern = tcv_kernel_dec<T, BITS, NMAT, NTOK>;
+    else
+        kern = tcv_kernel_wide<T, BITS, NMAT, NTOK>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return LQ_E_CUDA;
     cudaLaunchConfig_t cfg = {};
