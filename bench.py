@@ -326,6 +326,21 @@ def bench_moe(torch, M, steps, warmup, dev, stream):
             "gbs": by / (ms * 1e-3) / 1e9}
 
 
+def bench_norm(torch, steps, warmup, dev, stream, rows=8192, D=4096):
+    """The fused residual add + RMS norm over rows x D bf16 (x, r read; h, n written; w cached): GB/s."""
+    from locals_b200 import norm
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5)
+    x = torch.randn((rows, D), generator=gen, device=dev).to(torch.bfloat16)
+    r = torch.randn((rows, D), generator=gen, device=dev).to(torch.bfloat16)
+    w = torch.randn((D,), generator=gen, device=dev).to(torch.bfloat16)
+    g = capture(torch, lambda: norm.add_rms(x, r, w, 1e-6), stream)
+    ms = timed(torch, g.replay, steps, warmup, stream)
+    by = 4 * rows * D * 2 + D * 2
+    return {"rows": rows, "D": D, "us": ms * 1e3, "GB/s": by / (ms * 1e-3) / 1e9}
+
+
 def bench_prefill(torch, steps, warmup, dev, stream):
     """Config 5: x bf16 [2048, 4096] . 4-bit [14336, 4096]^T -> TFLOP/s."""
     from locals_b200 import kernels
@@ -497,6 +512,9 @@ def run_gpu(args):
         r = bench_prefill(torch, 3, args.warmup, dev, stream)
         extra["cfg5_prefill"] = {"TFLOP/s": round(r["tflops"], 1), "frac_bf16": round(r["tflops"] / tfl, 3),
                                  "ms": round(r["ms"], 3)}
+        r = bench_norm(torch, args.steps, args.warmup, dev, stream)
+        extra["add_rms_norm_8192x4096"] = {"GB/s": round(r["GB/s"], 1), "frac_hbm": round(r["GB/s"] / hbm, 3),
+                                           "us": round(r["us"], 2)}
 
     if ws > 1 and not args.quick:
         extra.update(bench_sharded(torch, dist, ws, max(5, args.steps // 2), args.warmup, dev, stream))

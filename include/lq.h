@@ -127,6 +127,25 @@ int lq_moe_experts(const void* xs, const int32_t* starts, const int32_t* experts
 int lq_moe_combine(const void* ys, const float* weights, const int32_t* pos, void* y, int T, int k, int D, int dtype,
                    void* stream);
 
+/* h = x + r (rounded to dtype) and n = w * rms_norm(h) in one pass over rows of D values, the sum of squares
+ * in fp32: n = T(w * T(h * 1/sqrt(mean(h^2) + eps))). Replaces norm_kernel.add_rms (locals/norm_kernel.py:73-85),
+ * the residual add and input norm between a decoder layer's projections. D % 8 == 0, D <= 8192; x, r, w, h,
+ * n 16-byte aligned. */
+int lq_add_rms_norm(const void* x, const void* r, const void* w, void* h, void* n, int rows, int D, float eps,
+                    int dtype, void* stream);
+
+/* The MoE combine with the shared expert, the layer's residual add and the next layer's input norm in one
+ * pass (locals/moe.py:353-389): y[t] = T(res[t] + T(T(sum_r weights[t,r] * ys[pos[t*k + r]]) + shared[t])),
+ * n[t] = T(nw * T(y[t] / sqrt(mean(y[t]^2) + eps))). shared == NULL: no shared expert; pos == NULL: row
+ * t*k + r. Same shape rules as lq_add_rms_norm. */
+int lq_moe_combine_norm(const void* ys, const float* weights, const int32_t* pos, const void* shared, const void* res,
+                        const void* nw, void* y, void* n, int T, int k, int D, float eps, int dtype, void* stream);
+
+/* Row packing's scatter (locals/kernels.py:840-851): dst (dst_rows, N) is zeroed, then dst row idx[j] = src row j
+ * for j < R. The gather half is lq_moe_gather(x, idx, R, 1, N, xs). N * 2 % 16 == 0. */
+int lq_scatter_rows(const void* src, const int32_t* idx, int R, int N, void* dst, int dst_rows, int dtype,
+                    void* stream);
+
 /* 1 if kernel family `family` (LQ_FAM_*; LQ_FAM_AUTO = any) accepts this shape and format, else 0. Host-only,
  * needs no GPU. Replaces the per-family supported(M, K, N, cfg) predicates the reference's tuner filters
  * its candidates with (locals/qmv_frag.py:162,519; locals/nax_kernel.py:399-408; locals/kernels.py:654-674). */

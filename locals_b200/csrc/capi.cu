@@ -42,6 +42,13 @@ int tcvp_run(const void* x, int M, const QmvMats& mats, int nmat, int N, int K, 
 int tcvp_run_grouped(const void* xs, int P, const QmvMats& mats, int nmat, int N, int K, void* out,
                      const int32_t* starts, const int32_t* experts, const int32_t* nseg, int E, int bits, int dtype,
                      int ntok, cudaStream_t st);
+bool norm_shape_ok(int D);
+int add_rms_run(const void* x, const void* r, const void* w, void* h, void* n, int rows, int D, float eps, int dtype,
+                cudaStream_t st);
+int combine_norm_run(const void* ys, const float* wts, const int32_t* pos, const void* shared, const void* res,
+                     const void* nw, void* y, void* n, int T, int K, int D, float eps, int dtype, cudaStream_t st);
+int scatter_rows_run(const void* src, const int32_t* idx, int R, int row_bytes, void* dst, int dst_rows,
+                     cudaStream_t st);
 }  // namespace lq
 
 using namespace lq;
@@ -338,6 +345,42 @@ int lq_moe_experts(const void* xs, const int32_t* starts, const int32_t* experts
     const int nseg_grid = (E + 1) < P ? (E + 1) : P;  // (one more for a padding bucket, expert id E)
     return finish(qmv_run(xs, gather_order ? 1 : P, m, glu ? 2 : 1, a, bits, dtype, nullptr, max_rows, nseg_grid,
                           reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int lq_add_rms_norm(const void* x, const void* r, const void* w, void* h, void* n, int rows, int D, float eps,
+                    int dtype, void* stream) {
+    if (!x || !r || !w || !h || !n) return LQ_E_ARG;
+    if (!is16(dtype)) return LQ_E_UNSUPPORTED;
+    if (rows < 1 || !norm_shape_ok(D) || !(eps >= 0.0f)) return LQ_E_SHAPE;
+    if (!aligned(x, 16) || !aligned(r, 16) || !aligned(w, 16) || !aligned(h, 16) || !aligned(n, 16)) return LQ_E_ALIGN;
+    int rc = check_device();
+    if (rc) return rc;
+    return finish(add_rms_run(x, r, w, h, n, rows, D, eps, dtype, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int lq_moe_combine_norm(const void* ys, const float* weights, const int32_t* pos, const void* shared, const void* res,
+                        const void* nw, void* y, void* n, int T, int k, int D, float eps, int dtype, void* stream) {
+    if (!ys || !weights || !res || !nw || !y || !n) return LQ_E_ARG;
+    if (!is16(dtype)) return LQ_E_UNSUPPORTED;
+    if (T < 1 || k < 1 || !norm_shape_ok(D) || !(eps >= 0.0f)) return LQ_E_SHAPE;
+    if (!aligned(ys, 16) || !aligned(res, 16) || !aligned(nw, 16) || !aligned(y, 16) || !aligned(n, 16) ||
+        (shared && !aligned(shared, 16)))
+        return LQ_E_ALIGN;
+    int rc = check_device();
+    if (rc) return rc;
+    return finish(combine_norm_run(ys, weights, pos, shared, res, nw, y, n, T, k, D, eps, dtype,
+                                   reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int lq_scatter_rows(const void* src, const int32_t* idx, int R, int N, void* dst, int dst_rows, int dtype,
+                    void* stream) {
+    if (!src || !idx || !dst) return LQ_E_ARG;
+    if (!is16(dtype)) return LQ_E_UNSUPPORTED;
+    if (R < 0 || N < 1 || dst_rows < 1 || (N * 2) % 16) return LQ_E_SHAPE;
+    if (!aligned(src, 16) || !aligned(dst, 16)) return LQ_E_ALIGN;
+    int rc = check_device();
+    if (rc) return rc;
+    return finish(scatter_rows_run(src, idx, R, N * 2, dst, dst_rows, reinterpret_cast<cudaStream_t>(stream)));
 }
 
 int lq_supported(int family, int M, int N, int K, int bits, int group_size, int dtype) {

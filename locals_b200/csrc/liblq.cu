@@ -7,4 +7,5 @@
 #include "tcvp.cu"
 #include "moe.cu"
 #include "tc_gemm.cu"
+#include "norm.cu"
 #include "capi.cu"

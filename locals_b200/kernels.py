@@ -204,6 +204,80 @@ def supported(family: str, M: int, K: int, N: int, bits: int = 4, dtype: torch.d
 
 # ---- a quantized linear layer ----------------------------------------------------------------------
 
+# ---- row packing of right-padded batches (locals/kernels.py:809-851) --------------------------------
+
+_PACK = threading.local()  # .ctx: (B, L, valid flat row indices int32 (R,), R) while a packed_rows block is active
+
+
+class packed_rows:
+    """While active, a QuantizedLinear applied to right-padded (B, L, K) activations computes only the valid
+    rows (lengths[b] of row block b) and scatters them back, zeros elsewhere -- padding costs no matmul work
+    (the reference's ``packed_rows``, locals/kernels.py:814-830). The gather and scatter are the library's
+    row kernels (``lq_moe_gather`` with k = 1, ``lq_scatter_rows``)."""
+
+    def __init__(self, B: int, L: int, lengths: Sequence[int], device=None):
+        idx = [b * L + i for b, n in enumerate(lengths) for i in range(int(n))]
+        self.ctx = (B, L, torch.tensor(idx, dtype=torch.int32, device=device or "cuda"), len(idx))
+
+    def __enter__(self):
+        self.prev = getattr(_PACK, "ctx", None)
+        _PACK.ctx = self.ctx
+        return self
+
+    def __exit__(self, *a):
+        _PACK.ctx = self.prev
+
+
+def gather_rows(x2: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+    """x2[idx] for a (rows, K) matrix (16-byte rows)."""
+    R, K = idx.numel(), x2.shape[-1]
+    xs = torch.empty((R, K), dtype=x2.dtype, device=x2.device)
+    if R:
+        call("lq_moe_gather", x2.data_ptr(), idx.data_ptr(), R, 1, K, xs.data_ptr(), _stream())
+    return xs
+
+
+def scatter_rows(ys: torch.Tensor, idx: torch.Tensor, rows: int) -> torch.Tensor:
+    """A (rows, N) matrix of zeros with row idx[j] = ys[j]."""
+    N = ys.shape[-1]
+    y = torch.empty((rows, N), dtype=ys.dtype, device=ys.device)
+    call("lq_scatter_rows", ys.data_ptr(), idx.data_ptr(), idx.numel(), N, y.data_ptr(), rows, dtype_code(ys.dtype),
+         _stream())
+    return y
+
+
+def _maybe_packed(x: torch.Tensor, fn: Callable) -> torch.Tensor:
+    ctx = getattr(_PACK, "ctx", None)
+    if ctx is not None and x.dim() == 3 and x.shape[0] == ctx[0] and x.shape[1] == ctx[1] and ctx[3] < ctx[0] * ctx[1]:
+        B, L, idx, R = ctx
+        xs = gather_rows(x.reshape(B * L, -1).contiguous(), idx)
+        ys = fn(xs)
+        return scatter_rows(ys, idx, B * L).reshape(B, L, -1)
+    return fn(x)
+
+
+def pad_rows(N: int, K: int, M: int, dtype: torch.dtype, bits: int = 4) -> int:
+    """The rows to compute M rows of this shape at (the reference's ``_pad_rows``, locals/kernels.py:764-794):
+    up to 2M rows where the tuner's recorded times say the shape runs at least 7% faster there (8 to 16 rows
+    unless LOCALS_PAD_ROWS=all; LOCALS_PAD_ROWS=0 never pads)."""
+    import os
+
+    from . import tune
+
+    mode = os.environ.get("LOCALS_PAD_ROWS", "1")
+    if mode == "0" or not (8 <= M <= 16 or mode == "all"):
+        return M
+    tm = tune.best_time(N, K, M, dtype, bits)
+    best, bt = M, tm
+    if tm is None:
+        return M
+    for m2 in range(M + 1, min(MAX_SMALL_M, 2 * M) + 1):
+        t2 = tune.best_time(N, K, m2, dtype, bits)
+        if t2 is not None and t2 < 0.93 * tm and t2 < bt:
+            best, bt = m2, t2
+    return best
+
+
 class QuantizedLinear:
     """MLX QuantizedLinear's tensors (weight uint32 (N, K*bits/32), scales, biases (N, K/64)) with the
     reference's routing (locals/kernels.py:1031-1054): the tuned choice for (N, K, M, dtype) if one is
@@ -223,12 +297,23 @@ class QuantizedLinear:
         return self.weight.shape[1] * 32 // self.bits
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        return _maybe_packed(x, self._call)
+
+    def _call(self, x: torch.Tensor) -> torch.Tensor:
         from . import tune
 
-        M = x.numel() // x.shape[-1]
-        choice = tune.lookup(self.out_features, self.in_features, M, x.dtype, self.bits)
-        y = quantized_matmul(x, self.weight, self.scales, self.biases, group_size=self.group_size, bits=self.bits,
-                             choice=choice)
+        K = x.shape[-1]
+        M = x.numel() // K
+        P = pad_rows(self.out_features, K, M, x.dtype, self.bits)
+        if P > M:  # more rows run faster for this shape: compute them, keep these
+            x2 = torch.cat([x.reshape(M, K), x.new_zeros((P - M, K))])
+            choice = tune.lookup(self.out_features, K, P, x.dtype, self.bits)
+            y = quantized_matmul(x2, self.weight, self.scales, self.biases, group_size=self.group_size,
+                                 bits=self.bits, choice=choice)[:M].reshape(*x.shape[:-1], -1)
+        else:
+            choice = tune.lookup(self.out_features, K, M, x.dtype, self.bits)
+            y = quantized_matmul(x, self.weight, self.scales, self.biases, group_size=self.group_size, bits=self.bits,
+                                 choice=choice)
         if self.bias is not None:
             y = y + self.bias
         return y

@@ -101,6 +101,22 @@ def combine(ys: torch.Tensor, weights: torch.Tensor, pos: Optional[torch.Tensor]
     return y
 
 
+def combine_norm(ys: torch.Tensor, weights: torch.Tensor, pos: Optional[torch.Tensor], res: torch.Tensor,
+                 nw: torch.Tensor, eps: float, shared: Optional[torch.Tensor] = None) -> tuple:
+    """The combine, the shared expert's output, the layer's residual add and the next layer's input norm in one
+    kernel (locals/moe.py:353-389): (y, n) with y = res + combine(...) (+ shared), n = rms_norm(y) * nw."""
+    T, k = weights.shape
+    D = ys.shape[-1]
+    y = torch.empty((T, D), dtype=ys.dtype, device=ys.device)
+    n = torch.empty((T, D), dtype=ys.dtype, device=ys.device)
+    sh = None if shared is None else shared.reshape(T, D).contiguous()
+    rs = res.reshape(T, D).contiguous()
+    call("lq_moe_combine_norm", ys.data_ptr(), weights.data_ptr(), None if pos is None else pos.data_ptr(),
+         None if sh is None else sh.data_ptr(), rs.data_ptr(), nw.data_ptr(), y.data_ptr(), n.data_ptr(), T, k, D,
+         float(eps), dtype_code(ys.dtype), _stream())
+    return y, n
+
+
 GATHER_IN_KERNEL_MAX_ROWS = 16  # up to this many tokens the GLU kernel fetches the pairs' tokens itself
 
 

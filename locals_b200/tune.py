@@ -21,6 +21,7 @@ import torch
 
 _LOCK = threading.RLock()
 _CHOICE: dict = {}
+_TIMES: dict = {}  # key -> ms per call of the chosen candidate (the cache's "__times__", as the reference keeps)
 _LOADED = False
 
 
@@ -48,12 +49,22 @@ def _load() -> None:
         for k, v in data.items():
             if isinstance(v, list) and v and isinstance(v[0], str):
                 _CHOICE[k] = tuple(v)
+        times = data.get("__times__")
+        if isinstance(times, dict):
+            _TIMES.update({k: float(v) for k, v in times.items() if isinstance(v, (int, float))})
 
 
 def lookup(N: int, K: int, M: int, dtype: torch.dtype, bits: int = 4) -> Optional[tuple]:
     if not _LOADED:
         _load()
     return _CHOICE.get(_key(N, K, M, dtype, bits))
+
+
+def best_time(N: int, K: int, M: int, dtype: torch.dtype, bits: int = 4) -> Optional[float]:
+    """ms per call of the tuned choice for this shape, if the tuner has timed it (pad_rows reads it)."""
+    if not _LOADED:
+        _load()
+    return _TIMES.get(_key(N, K, M, dtype, bits))
 
 
 def save() -> None:
@@ -67,6 +78,9 @@ def save() -> None:
         except (OSError, ValueError):
             data = {}
         data.update({k: list(v) for k, v in _CHOICE.items()})
+        times = data.get("__times__") if isinstance(data.get("__times__"), dict) else {}
+        times.update(_TIMES)
+        data["__times__"] = times
         fd, tmp = tempfile.mkstemp(dir=os.path.dirname(path), suffix=".tmp")
         try:
             with os.fdopen(fd, "w") as f:
@@ -123,6 +137,8 @@ def choose(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch
     if best is None:
         raise RuntimeError("no candidate kernel passed the correctness gate")
     set_choice(N, K, M, x.dtype, bits, best)
+    with _LOCK:
+        _TIMES[_key(N, K, M, x.dtype, bits)] = best_t
     if persist:
         save()
     return best

@@ -335,3 +335,42 @@ void lqo_combine(const float* ys, const float* w, int64_t T, int k, int64_t D, f
             y[t * D + d] = acc;
         }
 }
+
+/* Residual add + RMS norm (locals/norm_kernel.py:16-85): h = round(x + r); n = round(w * round(h * inv)) with
+ * inv = 1 / sqrt(sum(h^2) / D + eps), the sum of squares in float32. Inputs hold values already in dtype. */
+void lqo_add_rms(const float* x, const float* r, const float* w, int64_t rows, int64_t D, float eps, int dtype,
+                 float* h, float* n) {
+    for (int64_t t = 0; t < rows; t++) {
+        float sq = 0.0f;
+        for (int64_t d = 0; d < D; d++) {
+            const float v = lqo_round1(x[t * D + d] + r[t * D + d], dtype);
+            h[t * D + d] = v;
+            sq += v * v;
+        }
+        const float inv = 1.0f / sqrtf(sq / (float)D + eps);
+        for (int64_t d = 0; d < D; d++)
+            n[t * D + d] = lqo_round1(w[d] * lqo_round1(h[t * D + d] * inv, dtype), dtype);
+    }
+}
+
+/* The MoE combine with the shared expert, the layer's residual add and the next norm (locals/moe.py:353-389):
+ * y = round(sum_k weights[t,k] * ys[t*k+k]) (float32, slots in order); if shared: y = round(y + shared);
+ * y = round(res + y); n as lqo_add_rms with nw. ys rows in slot order (row t*k + r); shared may be NULL. */
+void lqo_combine_norm(const float* ys, const float* w, const float* shared, const float* res, const float* nw,
+                      int64_t T, int k, int64_t D, float eps, int dtype, float* y, float* n) {
+    for (int64_t t = 0; t < T; t++) {
+        float sq = 0.0f;
+        for (int64_t d = 0; d < D; d++) {
+            float acc = 0.0f;
+            for (int r = 0; r < k; r++) acc += ys[(t * k + r) * D + d] * w[t * k + r];
+            float v = lqo_round1(acc, dtype);
+            if (shared) v = lqo_round1(v + shared[t * D + d], dtype);
+            v = lqo_round1(res[t * D + d] + v, dtype);
+            y[t * D + d] = v;
+            sq += v * v;
+        }
+        const float inv = 1.0f / sqrtf(sq / (float)D + eps);
+        for (int64_t d = 0; d < D; d++)
+            n[t * D + d] = lqo_round1(nw[d] * lqo_round1(y[t * D + d] * inv, dtype), dtype);
+    }
+}

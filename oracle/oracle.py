@@ -45,6 +45,9 @@ def lib():
         L.lqo_group.argtypes = [u32p, i64, ci, i32p, i32p, i32p, i32p]
         L.lqo_swiglu.argtypes = [f32p, f32p, i64, ci, f32p]
         L.lqo_combine.argtypes = [f32p, f32p, i64, ci, i64, f32p]
+        L.lqo_add_rms.argtypes = [f32p, f32p, f32p, i64, i64, ctypes.c_float, ci, f32p, f32p]
+        L.lqo_combine_norm.argtypes = [f32p, f32p, ctypes.c_void_p, f32p, f32p, i64, ci, i64, ctypes.c_float, ci,
+                                       f32p, f32p]
         L.lqo_round.argtypes = [f32p, i64, ci]
         _lib = L
     return _lib
@@ -171,6 +174,34 @@ def combine(ys, w) -> np.ndarray:
     y = np.zeros((T, D), np.float32)
     lib().lqo_combine(ys, w, T, k, D, y)
     return y
+
+
+def add_rms(x, r, w, eps, dtype):
+    """(h, n) of the fused residual add + RMS norm (norm_kernel.add_rms)."""
+    x, r, w = _f32(x), _f32(r), _f32(w)
+    rows, D = x.shape
+    h = np.zeros_like(x)
+    n = np.zeros_like(x)
+    lib().lqo_add_rms(x, r, w, rows, D, eps, _DT[dtype], h, n)
+    return h, n
+
+
+def combine_norm(ys, w, res, nw, eps, dtype, shared=None):
+    """(y, n): the MoE combine + shared expert + residual add + RMS norm (moe.py:353-389); ys (T*k, D) in
+    slot order."""
+    w = _f32(w)
+    T, k = w.shape
+    ys = _f32(ys).reshape(T * k, -1)
+    D = ys.shape[1]
+    res, nw = _f32(res), _f32(nw)
+    y = np.zeros((T, D), np.float32)
+    n = np.zeros((T, D), np.float32)
+    sh = None
+    if shared is not None:
+        shared = _f32(shared)
+        sh = shared.ctypes.data_as(ctypes.c_void_p)
+    lib().lqo_combine_norm(ys, w, sh, res, nw, T, k, D, eps, _DT[dtype], y, n)
+    return y, n
 
 
 def linear(x, q, dtype) -> np.ndarray:
