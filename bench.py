@@ -341,6 +341,25 @@ def bench_norm(torch, steps, warmup, dev, stream, rows=8192, D=4096):
     return {"rows": rows, "D": D, "us": ms * 1e3, "GB/s": by / (ms * 1e-3) / 1e9}
 
 
+def bench_kv(torch, steps, warmup, dev, stream, B=8, n=32768):
+    """8-bit KV decode attention over a Flint full-attention layer's cache (32 query heads on 4 key/value heads,
+    head dim 128, sinks) at n keys a row: GB/s of the cache read (272 bytes a key and kv head; > L2 at B*n = 2^18)."""
+    from locals_b200 import qkv
+
+    H, KVH = 32, 4
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(6)
+    keys = qkv.quantize((torch.randn((B, KVH, n, 128), generator=gen, device=dev) * 2).to(torch.bfloat16))
+    values = qkv.quantize(torch.randn((B, KVH, n, 128), generator=gen, device=dev).to(torch.bfloat16))
+    q = torch.randn((B, H, 1, 128), generator=gen, device=dev).to(torch.bfloat16)
+    sinks = (torch.randn((H,), generator=gen, device=dev) * 2).to(torch.bfloat16)
+    start = torch.zeros((B,), dtype=torch.int32, device=dev)
+    g = capture(torch, lambda: qkv.attend(q, keys, values, n, sinks, 0.0884, start), stream)
+    ms = timed(torch, g.replay, steps, warmup, stream)
+    by = B * KVH * n * 272 + 2 * B * H * 128 * 2
+    return {"B": B, "n": n, "us": ms * 1e3, "GB/s": by / (ms * 1e-3) / 1e9}
+
+
 def bench_prefill(torch, steps, warmup, dev, stream):
     """Config 5: x bf16 [2048, 4096] . 4-bit [14336, 4096]^T -> TFLOP/s."""
     from locals_b200 import kernels
@@ -515,6 +534,10 @@ def run_gpu(args):
         r = bench_norm(torch, args.steps, args.warmup, dev, stream)
         extra["add_rms_norm_8192x4096"] = {"GB/s": round(r["GB/s"], 1), "frac_hbm": round(r["GB/s"] / hbm, 3),
                                            "us": round(r["us"], 2)}
+        for B, n in ((8, 32768), (32, 8192)):
+            r = bench_kv(torch, args.steps, args.warmup, dev, stream, B, n)
+            extra[f"kv_attend_8bit_b{B}_n{n}"] = {"GB/s": round(r["GB/s"], 1), "frac_hbm": round(r["GB/s"] / hbm, 3),
+                                                  "us": round(r["us"], 2)}
 
     if ws > 1 and not args.quick:
         extra.update(bench_sharded(torch, dist, ws, max(5, args.steps // 2), args.warmup, dev, stream))

@@ -14,6 +14,7 @@
 #ifndef LQ_H_
 #define LQ_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -145,6 +146,21 @@ int lq_moe_combine_norm(const void* ys, const float* weights, const int32_t* pos
  * for j < R. The gather half is lq_moe_gather(x, idx, R, 1, N, xs). N * 2 % 16 == 0. */
 int lq_scatter_rows(const void* src, const int32_t* idx, int R, int N, void* dst, int dst_rows, int dtype,
                     void* stream);
+
+/* Decode attention over an 8-bit key/value cache, replacing qkv.attend (locals/qkv.py:213-249): for every row b
+ * and query head h, softmax over the keys at positions max(start[b], 0) .. n-1 and the head's sink logit
+ * (sinks[h], natural-log units; NULL = none) of scale * q.k, times the values; out = T(sum p v / sum p).
+ * q (B, H, head_dim) and out (B, H, head_dim) in dtype; the cache is read in place in the reference's layout:
+ * kq, vq uint32 (B, KVH, cap, head_dim/4) (MLX affine 8-bit, four codes a word, low byte first), ks, kb, vs, vb
+ * (B, KVH, cap, head_dim/64) in dtype. start may be NULL (every row from 0). head_dim == 128, H % KVH == 0,
+ * H / KVH <= 16, 0 <= n <= cap. workspace: lq_kv_attend_workspace(B, H, KVH, n) bytes (16-byte aligned; NULL
+ * when that is 0). */
+int lq_kv_attend(const void* q, const uint32_t* kq, const void* ks, const void* kb, const uint32_t* vq, const void* vs,
+                 const void* vb, const int32_t* start, int n, const float* sinks, float scale, int B, int H, int KVH,
+                 int cap, int head_dim, int dtype, void* workspace, size_t workspace_bytes, void* out, void* stream);
+
+/* Bytes of workspace lq_kv_attend needs for this shape on the current device (0: none). */
+size_t lq_kv_attend_workspace(int B, int H, int KVH, int n);
 
 /* 1 if kernel family `family` (LQ_FAM_*; LQ_FAM_AUTO = any) accepts this shape and format, else 0. Host-only,
  * needs no GPU. Replaces the per-family supported(M, K, N, cfg) predicates the reference's tuner filters

@@ -40,6 +40,9 @@ SIGNATURES = {
     "lq_add_rms_norm": ([_vp, _vp, _vp, _vp, _vp, _i, _i, ctypes.c_float, _i, _vp], _i),
     "lq_moe_combine_norm": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, ctypes.c_float, _i, _vp], _i),
     "lq_scatter_rows": ([_vp, _vp, _i, _i, _vp, _i, _i, _vp], _i),
+    "lq_kv_attend": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, ctypes.c_float, _i, _i, _i, _i, _i, _i, _vp,
+                      ctypes.c_size_t, _vp, _vp], _i),
+    "lq_kv_attend_workspace": ([_i, _i, _i, _i], ctypes.c_size_t),
     "lq_supported": ([_i, _i, _i, _i, _i, _i, _i], _i),
     "lq_list_configs": ([_i, _i, _i, _i, _i, _i, ctypes.POINTER(Cfg), _i], _i),
     "lq_device_status": ([_i], ctypes.c_uint),

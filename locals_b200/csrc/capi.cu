@@ -43,6 +43,12 @@ int tcvp_run_grouped(const void* xs, int P, const QmvMats& mats, int nmat, int N
                      const int32_t* starts, const int32_t* experts, const int32_t* nseg, int E, int bits, int dtype,
                      int ntok, cudaStream_t st);
 bool norm_shape_ok(int D);
+bool kv_attend_shape_ok(int B, int H, int KVH, int n, int cap, int head_dim);
+size_t kv_attend_workspace_bytes(int B, int H, int KVH, int n, int sms);
+int kv_attend_run(const void* q, const uint32_t* kq, const void* ks, const void* kb, const uint32_t* vq,
+                  const void* vs, const void* vb, const int32_t* start, int n, const float* sinks, float scale, int B,
+                  int H, int KVH, int cap, int dtype, void* workspace, size_t workspace_bytes, void* out,
+                  cudaStream_t st);
 int add_rms_run(const void* x, const void* r, const void* w, void* h, void* n, int rows, int D, float eps, int dtype,
                 cudaStream_t st);
 int combine_norm_run(const void* ys, const float* wts, const int32_t* pos, const void* shared, const void* res,
@@ -356,6 +362,28 @@ int lq_add_rms_norm(const void* x, const void* r, const void* w, void* h, void* 
     int rc = check_device();
     if (rc) return rc;
     return finish(add_rms_run(x, r, w, h, n, rows, D, eps, dtype, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+size_t lq_kv_attend_workspace(int B, int H, int KVH, int n) {
+    if (B < 1 || H < 1 || KVH < 1 || n < 0) return 0;
+    if (check_device() != LQ_OK) return 0;
+    return kv_attend_workspace_bytes(B, H, KVH, n, device_info().sm_count);
+}
+
+int lq_kv_attend(const void* q, const uint32_t* kq, const void* ks, const void* kb, const uint32_t* vq, const void* vs,
+                 const void* vb, const int32_t* start, int n, const float* sinks, float scale, int B, int H, int KVH,
+                 int cap, int head_dim, int dtype, void* workspace, size_t workspace_bytes, void* out, void* stream) {
+    if (!q || !kq || !ks || !kb || !vq || !vs || !vb || !out) return LQ_E_ARG;
+    if (!is16(dtype)) return LQ_E_UNSUPPORTED;
+    if (!kv_attend_shape_ok(B, H, KVH, n, cap, head_dim) || !(scale == scale)) return LQ_E_SHAPE;
+    if (!aligned(q, 16) || !aligned(kq, 16) || !aligned(vq, 16) || !aligned(ks, 4) || !aligned(kb, 4) ||
+        !aligned(vs, 4) || !aligned(vb, 4) || !aligned(out, 2) || !aligned(start, 4) || !aligned(sinks, 4) ||
+        !aligned(workspace, 16))
+        return LQ_E_ALIGN;
+    int rc = check_device();
+    if (rc) return rc;
+    return finish(kv_attend_run(q, kq, ks, kb, vq, vs, vb, start, n, sinks, scale, B, H, KVH, cap, dtype, workspace,
+                                workspace_bytes, out, reinterpret_cast<cudaStream_t>(stream)));
 }
 
 int lq_moe_combine_norm(const void* ys, const float* weights, const int32_t* pos, const void* shared, const void* res,

@@ -8,4 +8,5 @@
 #include "moe.cu"
 #include "tc_gemm.cu"
 #include "norm.cu"
+#include "kv_attend.cu"
 #include "capi.cu"

@@ -38,6 +38,11 @@
  *   lqo_swiglu        silu(g) * u with the rounding points of locals/moe.py:284-289.
  *   lqo_combine       sum_k w_k * y_k in float32, slots in their order
  *                     (locals/moe.py:339-348).
+ *   lqo_add_rms / lqo_combine_norm   locals/norm_kernel.py:16-85, locals/moe.py:353-389.
+ *   lqo_kv_attend     decode attention over an 8-bit key/value cache with sinks and left
+ *                     padding (locals/qkv.py:30-249): keys and values dequantized in float32
+ *                     (qkv.py:50-53), scores scale * q.k, softmax over the keys start[b] .. n-1
+ *                     and the head's sink (qkv.py:_PASS2), in double here.
  *
  * Build: oracle/build.py (gcc -O2 -fopenmp -shared).
  */
@@ -372,5 +377,53 @@ void lqo_combine_norm(const float* ys, const float* w, const float* shared, cons
         const float inv = 1.0f / sqrtf(sq / (float)D + eps);
         for (int64_t d = 0; d < D; d++)
             n[t * D + d] = lqo_round1(nw[d] * lqo_round1(y[t * D + d] * inv, dtype), dtype);
+    }
+}
+
+/* Decode attention over an 8-bit key/value cache (locals/qkv.py:30-249). q (B, H, HD) float; kq, vq uint32
+ * (B, KVH, cap, HD/4), four codes a word, low byte first; ks, kb, vs, vb (B, KVH, cap, HD/64) float. Query head
+ * h reads kv head h / (H / KVH). For row b the keys max(start[b], 0) .. n-1 (start NULL: from 0); element d of
+ * a key is the float32 s * code + b of its group (qkv.py:50-53); score = scale * sum_d q_d k_d; out = sum p v /
+ * (sum p + exp(sink - M)) with p = exp(score - M), M the largest of the scores and the sink (sinks NULL: no
+ * sink; qkv.py:_PASS2); 0 where nothing is attended. Double accumulation, out (B, H, HD) float. */
+void lqo_kv_attend(const float* q, const uint32_t* kq, const float* ks, const float* kb, const uint32_t* vq,
+                   const float* vs, const float* vb, const int32_t* start, int64_t n, const float* sinks, float scale,
+                   int64_t B, int64_t H, int64_t KVH, int64_t cap, int64_t HD, float* out) {
+    const int64_t G = H / KVH, WPR = HD / 4, GPR = HD / 64;
+#pragma omp parallel for schedule(dynamic)
+    for (int64_t bh = 0; bh < B * H; bh++) {
+        const int64_t b = bh / H, h = bh % H, kh = h / G;
+        const int64_t lo = start ? (start[b] > 0 ? start[b] : 0) : 0;
+        const float* qr = q + bh * HD;
+        const int64_t row0 = (b * KVH + kh) * cap;
+        const int64_t cnt = n > lo ? n - lo : 0;
+        double* sc = (double*)malloc((size_t)(cnt > 0 ? cnt : 1) * sizeof(double));
+        double* o = (double*)calloc((size_t)HD, sizeof(double));
+        double M = sinks ? (double)sinks[h] : -INFINITY;
+        for (int64_t t = 0; t < cnt; t++) {
+            const int64_t r = row0 + lo + t;
+            double acc = 0.0;
+            for (int64_t d = 0; d < HD; d++) {
+                const uint32_t code = (kq[r * WPR + d / 4] >> (8 * (d % 4))) & 0xffu;
+                const float k = ks[r * GPR + d / 64] * (float)code + kb[r * GPR + d / 64];
+                acc += (double)qr[d] * (double)k;
+            }
+            sc[t] = acc * (double)scale;
+            if (sc[t] > M) M = sc[t];
+        }
+        double L = (sinks && M > -INFINITY) ? exp((double)sinks[h] - M) : 0.0;
+        for (int64_t t = 0; t < cnt; t++) {
+            const int64_t r = row0 + lo + t;
+            const double p = exp(sc[t] - M);
+            L += p;
+            for (int64_t d = 0; d < HD; d++) {
+                const uint32_t code = (vq[r * WPR + d / 4] >> (8 * (d % 4))) & 0xffu;
+                const float v = vs[r * GPR + d / 64] * (float)code + vb[r * GPR + d / 64];
+                o[d] += p * (double)v;
+            }
+        }
+        for (int64_t d = 0; d < HD; d++) out[bh * HD + d] = L > 0.0 ? (float)(o[d] / L) : 0.0f;
+        free(sc);
+        free(o);
     }
 }

@@ -48,6 +48,8 @@ def lib():
         L.lqo_add_rms.argtypes = [f32p, f32p, f32p, i64, i64, ctypes.c_float, ci, f32p, f32p]
         L.lqo_combine_norm.argtypes = [f32p, f32p, ctypes.c_void_p, f32p, f32p, i64, ci, i64, ctypes.c_float, ci,
                                        f32p, f32p]
+        L.lqo_kv_attend.argtypes = [f32p, u32p, f32p, f32p, u32p, f32p, f32p, ctypes.c_void_p, i64, ctypes.c_void_p,
+                                    ctypes.c_float, i64, i64, i64, i64, i64, f32p]
         L.lqo_round.argtypes = [f32p, i64, ci]
         _lib = L
     return _lib
@@ -202,6 +204,24 @@ def combine_norm(ys, w, res, nw, eps, dtype, shared=None):
         sh = shared.ctypes.data_as(ctypes.c_void_p)
     lib().lqo_combine_norm(ys, w, sh, res, nw, T, k, D, eps, _DT[dtype], y, n)
     return y, n
+
+
+def kv_attend(q, keys, values, n: int, sinks, scale: float, start=None) -> np.ndarray:
+    """qkv.attend (locals/qkv.py:213-249) on the CPU: q (B, H, HD); keys / values = (words uint32 (B, KVH, cap,
+    HD/4), scales, biases (B, KVH, cap, HD/64)); sinks (H,) or None; start (B,) or None. Float32 (B, H, HD)."""
+    q = _f32(q)
+    B, H, HD = q.shape
+    kq = np.ascontiguousarray(keys[0], dtype=np.uint32)
+    vq = np.ascontiguousarray(values[0], dtype=np.uint32)
+    ks, kb, vs, vb = (_f32(a) for a in (keys[1], keys[2], values[1], values[2]))
+    KVH, cap = kq.shape[1], kq.shape[2]
+    st = None if start is None else np.ascontiguousarray(start, dtype=np.int32)
+    sk = None if sinks is None else _f32(sinks)
+    out = np.zeros((B, H, HD), np.float32)
+    lib().lqo_kv_attend(q, kq, ks, kb, vq, vs, vb, None if st is None else st.ctypes.data_as(ctypes.c_void_p), int(n),
+                        None if sk is None else sk.ctypes.data_as(ctypes.c_void_p), float(scale), B, H, KVH, cap, HD,
+                        out)
+    return out
 
 
 def linear(x, q, dtype) -> np.ndarray:

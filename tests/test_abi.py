@@ -14,7 +14,7 @@ HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))
 
 def declared():
     src = open(HEADER).read()
-    return sorted(set(re.findall(r"^(?:int|unsigned int|const char\*)\s+(lq_\w+)\s*\(", src, re.M)))
+    return sorted(set(re.findall(r"^(?:int|unsigned int|size_t|const char\*)\s+(lq_\w+)\s*\(", src, re.M)))
 
 
 def test_library_loads():
