@@ -28,6 +28,7 @@ extern "C" {
 #define LQ_E_UNSUPPORTED 4  /* bits / group size / dtype combination not built */
 #define LQ_E_CUDA 5         /* a CUDA runtime call failed (see lq_last_cuda_error) */
 #define LQ_E_DEVICE 6       /* the current device is not an sm_100 GPU */
+#define LQ_E_SCRATCH 7      /* the shape needs more scratch than lq_kv_attend_noalloc's fixed buffer holds */
 
 #define LQ_F16 0
 #define LQ_BF16 1
@@ -161,6 +162,19 @@ int lq_kv_attend(const void* q, const uint32_t* kq, const void* ks, const void* 
 
 /* Bytes of workspace lq_kv_attend needs for this shape on the current device (0: none). */
 size_t lq_kv_attend_workspace(int B, int H, int KVH, int n);
+
+/* lq_kv_attend without a workspace argument, for callers that cannot allocate device memory when they attend (a
+ * plugin given only raw device pointers, code inside a CUDA graph someone else built, a runtime whose memory pool is
+ * fixed at start-up). It has no counterpart in the reference, whose MLX kernels have outputs allocated for them.
+ * The per-block softmax parts go to a 4 MiB buffer inside the library (a __device__ array that every GPU loading
+ * the library holds until the process exits); nothing is allocated or freed. Shapes whose parts need more than
+ * 4 MiB (lq_kv_attend_workspace(B, H, KVH, n) > 4194304) return LQ_E_SCRATCH before any launch. The first call on a
+ * device looks up the buffer's device address (cudaGetSymbolAddress) and should come before any stream capture.
+ * All calls share the buffer: calls that overlap on the GPU (unordered streams) race and may return wrong
+ * results. Other arguments, results and errors as lq_kv_attend. */
+int lq_kv_attend_noalloc(const void* q, const uint32_t* kq, const void* ks, const void* kb, const uint32_t* vq,
+                         const void* vs, const void* vb, const int32_t* start, int n, const float* sinks, float scale,
+                         int B, int H, int KVH, int cap, int head_dim, int dtype, void* out, void* stream);
 
 /* 1 if kernel family `family` (LQ_FAM_*; LQ_FAM_AUTO = any) accepts this shape and format, else 0. Host-only,
  * needs no GPU. Replaces the per-family supported(M, K, N, cfg) predicates the reference's tuner filters

@@ -10,7 +10,7 @@ import threading
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "liblq.so")
 
-LQ_OK, LQ_E_ARG, LQ_E_SHAPE, LQ_E_ALIGN, LQ_E_UNSUPPORTED, LQ_E_CUDA, LQ_E_DEVICE = range(7)
+LQ_OK, LQ_E_ARG, LQ_E_SHAPE, LQ_E_ALIGN, LQ_E_UNSUPPORTED, LQ_E_CUDA, LQ_E_DEVICE, LQ_E_SCRATCH = range(8)
 F16, BF16, F32 = 0, 1, 2
 FAM_AUTO, FAM_QMV, FAM_TC, FAM_TCV = 0, 1, 2, 3
 
@@ -43,6 +43,8 @@ SIGNATURES = {
     "lq_kv_attend": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, ctypes.c_float, _i, _i, _i, _i, _i, _i, _vp,
                       ctypes.c_size_t, _vp, _vp], _i),
     "lq_kv_attend_workspace": ([_i, _i, _i, _i], ctypes.c_size_t),
+    "lq_kv_attend_noalloc": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, ctypes.c_float, _i, _i, _i, _i, _i, _i,
+                              _vp, _vp], _i),
     "lq_supported": ([_i, _i, _i, _i, _i, _i, _i], _i),
     "lq_list_configs": ([_i, _i, _i, _i, _i, _i, ctypes.POINTER(Cfg), _i], _i),
     "lq_device_status": ([_i], ctypes.c_uint),

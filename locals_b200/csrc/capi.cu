@@ -155,6 +155,7 @@ const char* lq_strerror(int code) {
         case LQ_E_UNSUPPORTED: return "unsupported bits/group/dtype";
         case LQ_E_CUDA: return "CUDA error";
         case LQ_E_DEVICE: return "not an sm_100 device";
+        case LQ_E_SCRATCH: return "shape needs more than the 4 MiB static scratch buffer";
         default: return "unknown";
     }
 }

@@ -10,3 +10,4 @@
 #include "norm.cu"
 #include "kv_attend.cu"
 #include "capi.cu"
+#include "kv_attend_noalloc.cu"
