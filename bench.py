@@ -589,6 +589,7 @@ CASES = {
     "tc": "prefill GEMM x bf16 [1024,4096] . 4-bit [7168,4096]^T",
     "moe16": "MoE layer, 64 experts top-4, D 2048, I 768, M=16",
     "moe512": "MoE layer, 64 experts top-4, D 2048, I 768, M=512",
+    "kv8": "8-bit KV decode attention, B=8, 32 query heads on 4 kv heads, 32768 keys (285 MB cache > L2)",
 }
 
 
@@ -634,6 +635,16 @@ def run_case(name):
         x = torch.randn((16 if name == "moe16" else 512, D), generator=gen, device=dev).to(torch.bfloat16)
         for _ in range(3):
             layer(x)
+    elif name == "kv8":
+        from locals_b200 import qkv
+
+        B, H, KVH, n = 8, 32, 4, 32768
+        keys = qkv.quantize((torch.randn((B, KVH, n, 128), generator=gen, device=dev) * 2).to(torch.bfloat16))
+        values = qkv.quantize(torch.randn((B, KVH, n, 128), generator=gen, device=dev).to(torch.bfloat16))
+        q = torch.randn((B, H, 1, 128), generator=gen, device=dev).to(torch.bfloat16)
+        sinks = (torch.randn((H,), generator=gen, device=dev) * 2).to(torch.bfloat16)
+        for _ in range(3):
+            qkv.attend(q, keys, values, n, sinks, 0.0884)
     else:
         raise SystemExit(f"unknown case {name}; known: {sorted(CASES)}")
     torch.cuda.synchronize()
