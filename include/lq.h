@@ -40,6 +40,9 @@ extern "C" {
 #define LQ_FAM_TC 2     /* prefill: dequant tiles into shared memory, tcgen05.mma into TMEM */
 #define LQ_FAM_TCV 3    /* tcgen05 with weights dequantized into TMEM (A operand), tokens as N;
                            p = {NTOK, KS, WS, PERSISTENT (1: one CTA per SM walks the tiles)} */
+#define LQ_FAM_QMVG 4   /* dense 4-bit decode, M <= 16, K % 256 == 0: each warp takes one 64-wide group of every
+                           stage for all of its CTA's 16-row fragments, fragments spread over every SM;
+                           p = {FR (max fragments a CTA, <= 4), NS} */
 
 typedef struct lq_cfg {
     int family;  /* LQ_FAM_* */

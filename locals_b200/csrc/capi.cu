@@ -43,6 +43,9 @@ int tcvp_run_grouped(const void* xs, int P, const QmvMats& mats, int nmat, int N
                      const int32_t* starts, const int32_t* experts, const int32_t* nseg, int E, int bits, int dtype,
                      int ntok, cudaStream_t st);
 bool norm_shape_ok(int D);
+bool qmvg_shape_ok(int M, int K, int bits);
+int qmvg_run(const void* x, const uint32_t* w, const void* s, const void* b, int nout, void* const* outs,
+             const int* seg_end, const int* ldo, int M, int N, int K, int dtype, const int* p, cudaStream_t st);
 bool kv_attend_shape_ok(int B, int H, int KVH, int n, int cap, int head_dim);
 size_t kv_attend_workspace_bytes(int B, int H, int KVH, int n, int sms);
 int kv_attend_run(const void* q, const uint32_t* kq, const void* ks, const void* kb, const uint32_t* vq,
@@ -124,6 +127,10 @@ static int qmm_common(const void* x, const uint32_t* w, const void* s, const voi
         if (nout != 1) return LQ_E_UNSUPPORTED;
         if (!tc_shape_ok(M, N, K, bits)) return LQ_E_SHAPE;
         return finish(tc_run(x, w, s, b, outs[0], M, N, K, bits, dtype, cfg ? cfg->p : nullptr, st));
+    }
+    if (fam == LQ_FAM_QMVG) {
+        if (!qmvg_shape_ok(M, K, bits)) return LQ_E_SHAPE;
+        return finish(qmvg_run(x, w, s, b, nout, outs, a.seg_end, a.ldo, M, N, K, dtype, cfg->p, st));
     }
     const QmvMats mats = one_matrix(w, s, b, N);
     if (fam == LQ_FAM_TCV) {
@@ -416,9 +423,11 @@ int lq_supported(int family, int M, int N, int K, int bits, int group_size, int 
     if (!is16(dtype) || (bits != 4 && bits != 8) || group_size != 64) return 0;
     if (M < 1 || N < 1 || K < 64 || K % 64) return 0;
     const bool qmv = qmv_shape_ok(K, bits), tcv = tcv_shape_ok(M, K, bits), tc = tc_shape_ok(M, N, K, bits);
+    const bool qmvg = qmvg_shape_ok(M, K, bits);
     switch (family) {
-        case LQ_FAM_AUTO: return (qmv || tcv || (M > 64 && tc)) ? 1 : 0;
+        case LQ_FAM_AUTO: return (qmv || qmvg || tcv || (M > 64 && tc)) ? 1 : 0;
         case LQ_FAM_QMV: return qmv ? 1 : 0;
+        case LQ_FAM_QMVG: return qmvg ? 1 : 0;
         case LQ_FAM_TCV: return tcv ? 1 : 0;
         case LQ_FAM_TC: return tc ? 1 : 0;
         default: return 0;
@@ -453,6 +462,10 @@ int lq_list_configs(int M, int N, int K, int bits, int group_size, int dtype, lq
                     if (ks <= nchunk) add(LQ_FAM_QMV, mt, wk, ks, 0);
             }
         }
+    }
+    if (lq_supported(LQ_FAM_QMVG, M, N, K, bits, group_size, dtype)) {
+        add(LQ_FAM_QMVG, 0, 0, 0, 0);
+        for (int fr = 1; fr <= 4; ++fr) add(LQ_FAM_QMVG, fr, 0, 0, 0);
     }
     if (lq_supported(LQ_FAM_TCV, M, N, K, bits, group_size, dtype)) {
         add(LQ_FAM_TCV, 0, 0, 0, 0);

@@ -3,6 +3,7 @@
 #include "lq_host.cu"
 #include "quant.cu"
 #include "qmv.cu"
+#include "qmvg.cu"
 #include "tcv.cu"
 #include "tcvp.cu"
 #include "moe.cu"

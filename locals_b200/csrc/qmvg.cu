@@ -1,0 +1,420 @@
+// Dense 4-bit decode, one 64-wide quantization group per warp ("qmvg" family): y (M, N) = x (M, K) . dequant(W)^T for
+// M <= 16 tokens, the shape of the fused QKV projection and of every 4-bit decode projection.
+//
+// Why a second decode kernel. In the row-split qmv kernel each warp owns 16 weight rows and walks K, so every warp
+// loads and permutes its own copy of each x slice and a CTA holds 64 rows, which leaves a third of the 148 SMs idle on
+// the 6144-row QKV matrix. Here the work is split the other way:
+//  * Rows: the N/16 row fragments are dealt out evenly over the CTAs (CTA c takes fragments [c*F/C, (c+1)*F/C)), so
+//    the QKV matrix's 384 fragments run 2 or 3 to an SM on all 148 SMs. Every CTA holds FR or FR - 1 fragments.
+//  * K: a ring stage holds 512 K values (8 groups) of all of the CTA's rows. Consumer warp w takes group w of every
+//    stage for ALL the CTA's fragments: it loads and permutes its x fragments once (two 16-byte loads and 8 prmt a
+//    token tile) and reuses them for every fragment. The eight warps' partial sums are added through shared memory
+//    at the end (no global scratch, no atomics).
+//  * A lane reads 8 bytes (16 codes) of a row per group, so all four lanes of an MMA k-slice hold codes of the same
+//    group; codes are dequantized straight into m16n8k16 A fragments (magic exponent: 128 + q exact in bf16, 1024 + q
+//    in fp16; one subtract and one fma with the group's scale and bias -- the weight rounded once to the activation
+//    dtype, as mx.dequantize rounds it). Tokens sit on the MMA's n side (Y^T = W X^T, the idea of the reference's
+//    locals/qmv_frag.py:1-19); lane t's codes (p, p + 4) of word 2t + (s >> 1) meet x values 16t + 8(s >> 1) + p,
+//    + p + 4 of the same group, which is the permutation applied to x.
+//  * One producer warp: one TMA box a stage for the packed words of all the CTA's rows ([128-byte segment][16 nf rows]
+//    [2 segments], 128-byte swizzle, L2 evict-first), cp.async for x (only the M real token rows, written in the same
+//    swizzled layout) and for scales and biases (zero-filled past K and past N). The SM's TMA unit spends about the
+//    same time on a 4 KB box as on a 16 KB one (measured on B200), so the kernel issues as few boxes as it can: one a
+//    stage. The weight boxes of the first stages are issued before griddepcontrol.wait, so under programmatic
+//    dependent launch they overlap the previous kernel; only x waits.
+// Reference: the multi-row GEMV it replaces, locals/qmv_multi.py:16-248 and locals/qmv_frag.py:34-540, behind
+// kernels._launcher (locals/kernels.py:516-576).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <type_traits>
+
+#include "lq_host.h"
+#include "lq_ptx.cuh"
+
+namespace lq {
+
+constexpr int QG_CW = 8;  // consumer warps: group w of every 8-group stage
+constexpr int QG_THREADS = 32 * (QG_CW + 1);
+constexpr int QG_MAX_STAGES = 6;
+constexpr int QG_MAX_FR = 4;
+
+template <int MT, int FR>
+struct QgShape {
+    static constexpr int MTOK = 8 * MT;                  // token slots
+    static constexpr int W_FRAG = 16 * 256;              // one 16-row fragment: 256 bytes (512 codes) a row
+    static constexpr int W_BYTES = FR * W_FRAG;
+    static constexpr int X_BYTES = 8 * MTOK * 128;       // 8 groups x MTOK tokens x 64 values (rows past M unused)
+    static constexpr int SB_BYTES = FR * 16 * 16;        // scales (or biases): rows x 8 groups x 2 bytes
+    static constexpr int STAGE_BYTES = (W_BYTES + X_BYTES + 2 * SB_BYTES + 1023) / 1024 * 1024;
+    static constexpr int RED_BYTES = QG_CW * MTOK * FR * 16 * 4;  // the warps' partial sums
+    static_assert(W_FRAG % 1024 == 0 && X_BYTES % 1024 == 0, "1 KB alignment of swizzled tiles");
+};
+
+struct QgArgs {
+    int M, N, K;
+    int kg;      // groups a row (K / 64)
+    int nchunk;  // stages of 512 K values
+    int nfrag;   // 16-row fragments (ceil(N / 16))
+    int ns;      // ring depth
+    int sb_vec;  // cp.async width for scale / bias rows
+    const void* x;
+    const void* s;
+    const void* b;
+    void* out[3];  // output column segments (fused q / k / v), or out[0] only
+    int seg_end[3];
+    int ldo[3];
+    int nseg_out;
+};
+
+__device__ __forceinline__ uint2 qg_lds64(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+
+// mma.sync m16n8k16 with fp32 accumulation, left to the compiler's scheduling (no side effects beyond its registers).
+template <typename T>
+__device__ __forceinline__ void qg_mma(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value)
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    else
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Output element (row, n) of the fused projection: segment chosen with constant indices (no local-memory copy of
+// the argument arrays).
+__device__ __forceinline__ void qg_store(const QgArgs& a, int row, int n, float v, bool bf16) {
+    void* base = a.out[0];
+    int start = 0, ld = a.ldo[0];
+    if (a.nseg_out > 1 && n >= a.seg_end[0]) {
+        const bool third = a.nseg_out > 2 && n >= a.seg_end[1];
+        base = third ? a.out[2] : a.out[1];
+        start = third ? a.seg_end[1] : a.seg_end[0];
+        ld = third ? a.ldo[2] : a.ldo[1];
+    }
+    const size_t off = size_t(row) * ld + (n - start);
+    if (bf16)
+        reinterpret_cast<__nv_bfloat16*>(base)[off] = __float2bfloat16_rn(v);
+    else
+        reinterpret_cast<__half*>(base)[off] = __float2half_rn(v);
+}
+
+template <typename T, int MT, int FR>
+__global__ void __launch_bounds__(QG_THREADS, 2)
+    qmvg_kernel(const __grid_constant__ CUtensorMap tm_w_full, const __grid_constant__ CUtensorMap tm_w_less,
+                const QgArgs a) {
+    using S = QgShape<MT, FR>;
+    using TR = F16Traits<T>;
+    constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+    constexpr int RING_MIN = S::RED_BYTES;  // the ring is reused for the partial sums
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int ns = a.ns;
+    const int ring = ns * S::STAGE_BYTES > RING_MIN ? ns * S::STAGE_BYTES : RING_MIN;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + ring);
+    uint64_t* empty = full + QG_MAX_STAGES;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int f0 = int((long long)blockIdx.x * a.nfrag / gridDim.x);
+    const int nf = int((long long)(blockIdx.x + 1) * a.nfrag / gridDim.x) - f0;  // FR or FR - 1 (host-chosen grid)
+    if (nf < 1 || nf > FR || nf < FR - 1) {  // the weight box has 16 FR or 16 (FR - 1) rows: nothing else fits
+        if (threadIdx.x == 0) record_status(LQ_DEV_BOUNDS);
+        return;
+    }
+    const int row0 = 16 * f0;
+    const int total = a.nchunk;
+    const int mv = a.M < S::MTOK ? a.M : S::MTOK;  // real token rows
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ns; ++s) {
+            mbar_init(&full[s], 1 + 32);  // lane 0's expect_tx arrive + 32 cp.async arrivals
+            mbar_init(&empty[s], QG_CW);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+    bool ok = true;
+
+    if (warp == QG_CW) {
+        // ------------------------------ producer warp ------------------------------
+        const uint64_t pol_w = policy_evict_first();
+        const CUtensorMap* tm_w = nf == FR ? &tm_w_full : &tm_w_less;  // box of 16 FR or 16 (FR - 1) rows
+        if (lane == 0) prefetch_tmap(tm_w);
+        const uint32_t smem_base = smem_u32(smem);
+        const int vb = a.sb_vec;
+        const int units = 16 / vb;
+        auto load_weights = [&](int c, int s) {
+            uint8_t* st = smem + s * S::STAGE_BYTES;
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&full[s], nf * S::W_FRAG);
+                tma_load_3d(st, tm_w, &full[s], 0, row0, 2 * c, pol_w);
+            }
+            const uint32_t sdst = smem_base + s * S::STAGE_BYTES + S::W_BYTES + S::X_BYTES;
+            const uint8_t* sbase = reinterpret_cast<const uint8_t*>(a.s);
+            const uint8_t* bbase = reinterpret_cast<const uint8_t*>(a.b);
+            for (int r = lane; r < nf * 16; r += 32) {
+                const int grow = row0 + r;
+                for (int u = 0; u < units; ++u) {
+                    const int gcol = 8 * c + u * (vb >> 1);
+                    const bool valid = grow < a.N && gcol < a.kg;
+                    const size_t off = valid ? (size_t(grow) * a.kg + gcol) * 2 : 0;
+                    const uint32_t d = sdst + r * 16 + u * vb;
+                    cp_async(d, sbase + off, vb, valid);
+                    cp_async(d + S::SB_BYTES, bbase + off, vb, valid);
+                }
+            }
+        };
+        // x values of stage c for the real token rows: 16-byte pieces, consecutive lanes along K (coalesced), written
+        // to [group][token][128 bytes] with piece p of token row r at p ^ (r & 7); zero past K
+        const uint8_t* xg = reinterpret_cast<const uint8_t*>(a.x);
+        auto load_x = [&](int c, int s) {
+            const uint32_t xdst = smem_base + s * S::STAGE_BYTES + S::W_BYTES;
+            for (int e = lane; e < 64 * mv; e += 32) {
+                const int tok = e >> 6, j = (e >> 3) & 7, p = e & 7;
+                const int k = (8 * c + j) * 64 + 8 * p;
+                const bool valid = k < a.K;
+                cp_async(xdst + j * (S::MTOK * 128) + tok * 128 + ((p ^ (tok & 7)) << 4),
+                         xg + (valid ? (size_t(tok) * a.K + k) * 2 : 0), 16, valid);
+            }
+        };
+        const int pre = total < ns ? total : ns;
+        for (int i = 0; i < pre; ++i) load_weights(i, i);
+        grid_dep_wait();  // x may be the previous kernel's output
+        for (int i = 0; i < pre; ++i) {
+            load_x(i, i);
+            cp_async_arrive(&full[i]);
+        }
+        if (lane == 0) grid_dep_launch();
+        for (int i = pre; i < total; ++i) {
+            const int s = i % ns;
+            ok = mbar_wait(&empty[s], ((i / ns) - 1) & 1);
+            if (!ok) break;
+            load_weights(i, s);
+            load_x(i, s);
+            cp_async_arrive(&full[s]);
+        }
+        __syncwarp();
+        return;
+    }
+
+    // ------------------------------ consumer warps ------------------------------
+    grid_dep_wait();  // (before any output store of this kernel)
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t smem_base = smem_u32(smem);
+    float acc[FR][MT][4];
+#pragma unroll
+    for (int f = 0; f < FR; ++f)
+#pragma unroll
+        for (int q = 0; q < MT; ++q)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[f][q][e] = 0.0f;
+
+    // this lane's 8 bytes of a row inside group w of a stage (128-byte swizzle: 16-byte chunk c of row r sits at
+    // c ^ (r & 7)); the stage's box is [segment][16 nf rows][128 bytes], fragment f's rows at 2048 f of each segment
+    const uint32_t w_off = (warp >> 2) * (nf * 2048) + g * 128 + (((2 * (warp & 3) + (t >> 1)) ^ g) << 4) + 8 * (t & 1);
+    const uint32_t x_off = warp * (S::MTOK * 128) + g * 128;
+    const uint32_t x_c0 = ((2 * t) ^ g) << 4, x_c1 = ((2 * t + 1) ^ g) << 4;
+
+    for (int i = 0; i < total; ++i) {
+        const int s = i % ns;
+        if (ok) ok = mbar_wait(&full[s], (i / ns) & 1);
+        if (ok && 8 * i + warp < a.kg) {
+            const uint32_t st = smem_base + s * S::STAGE_BYTES;
+            // x fragments of group w: values 16t .. 16t + 15 of tokens g (+ 8 mt), permuted to the code order
+            uint32_t xb[MT][4][2];
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                const uint32_t xr = st + S::W_BYTES + x_off + mt * 8 * 128;
+                const uint4 u0 = lds128(xr + x_c0), u1 = lds128(xr + x_c1);
+                xb[mt][0][0] = prmt(u0.x, u0.z, 0x5410);
+                xb[mt][0][1] = prmt(u0.x, u0.z, 0x7632);
+                xb[mt][1][0] = prmt(u0.y, u0.w, 0x5410);
+                xb[mt][1][1] = prmt(u0.y, u0.w, 0x7632);
+                xb[mt][2][0] = prmt(u1.x, u1.z, 0x5410);
+                xb[mt][2][1] = prmt(u1.x, u1.z, 0x7632);
+                xb[mt][3][0] = prmt(u1.y, u1.w, 0x5410);
+                xb[mt][3][1] = prmt(u1.y, u1.w, 0x7632);
+            }
+            const uint32_t sb = st + S::W_BYTES + S::X_BYTES + 2 * warp;
+#pragma unroll
+            for (int f = 0; f < FR; ++f) {
+                if (f < nf) {
+                    const uint32_t fb = st + f * 2048 + w_off;
+                    const uint2 wa = qg_lds64(fb), wb = qg_lds64(fb + 8 * 128);
+                    const int ra = 16 * f + g, rb = ra + 8;
+                    const uint32_t sa = lds_u16(sb + ra * 16), ba = lds_u16(sb + S::SB_BYTES + ra * 16);
+                    const uint32_t sbv = lds_u16(sb + rb * 16), bbv = lds_u16(sb + S::SB_BYTES + rb * 16);
+                    const uint32_t s2a = prmt(sa, sa, 0x1010), b2a = prmt(ba, ba, 0x1010);
+                    const uint32_t s2b = prmt(sbv, sbv, 0x1010), b2b = prmt(bbv, bbv, 0x1010);
+#pragma unroll
+                    for (int step = 0; step < 4; ++step) {
+                        const uint32_t va = step < 2 ? wa.x : wa.y, vbw = step < 2 ? wb.x : wb.y;
+                        const int sh = 8 * (step & 1);  // codes (p, p + 4) and (p + 1, p + 5), p = 2 (step & 1)
+                        const uint32_t a0 = TR::sub_magic_fma(lop3_and_or(va >> sh, 0x000F000Fu, TR::kMagic2), s2a, b2a);
+                        const uint32_t a2 =
+                            TR::sub_magic_fma(lop3_and_or(va >> (sh + 4), 0x000F000Fu, TR::kMagic2), s2a, b2a);
+                        const uint32_t a1 =
+                            TR::sub_magic_fma(lop3_and_or(vbw >> sh, 0x000F000Fu, TR::kMagic2), s2b, b2b);
+                        const uint32_t a3 =
+                            TR::sub_magic_fma(lop3_and_or(vbw >> (sh + 4), 0x000F000Fu, TR::kMagic2), s2b, b2b);
+#pragma unroll
+                        for (int mt = 0; mt < MT; ++mt)
+                            qg_mma<T>(acc[f][mt], a0, a1, a2, a3, xb[mt][step][0], xb[mt][step][1]);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+
+    // ---- the eight warps' partial sums, added through shared memory (the ring is free: every stage was consumed) ----
+    named_barrier(1, 32 * QG_CW);
+    float* red = reinterpret_cast<float*>(smem);  // [warp][token][FR * 16 rows]
+    constexpr int RR = FR * 16;
+#pragma unroll
+    for (int f = 0; f < FR; ++f)
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int row = 16 * f + g + 8 * (e >> 1), tok = 8 * mt + 2 * t + (e & 1);
+                red[(warp * S::MTOK + tok) * RR + row] = acc[f][mt][e];
+            }
+    named_barrier(1, 32 * QG_CW);
+    const int R = nf * 16;
+    for (int idx = threadIdx.x; idx < R * mv; idx += 32 * QG_CW) {
+        const int tok = idx / R, row = idx - tok * R;
+        const int n = row0 + row;
+        if (n >= a.N) continue;
+        float v = 0.0f;
+#pragma unroll
+        for (int w = 0; w < QG_CW; ++w) v += red[(w * S::MTOK + tok) * RR + row];
+        if (ok) qg_store(a, tok, n, v, kBF16);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// host side
+// ------------------------------------------------------------------------------------------------
+
+template <typename T, int MT, int FR>
+static int qmvg_launch_t(const void* x, const uint32_t* w, QgArgs a, int ns_req, int nctas, cudaStream_t st) {
+    using S = QgShape<MT, FR>;
+    const DeviceInfo& di = device_info();
+    const int K = a.K;
+    // stages: within half an SM's shared memory, so the next launch's CTA can start beside a running one
+    const size_t fixed = 2 * QG_MAX_STAGES * 8 + 1024;
+    const size_t budget = di.smem_per_sm / 2 - 1024;
+    int ns = int((budget - fixed) / S::STAGE_BYTES);
+    if (ns > QG_MAX_STAGES) ns = QG_MAX_STAGES;
+    if (ns > a.nchunk) ns = a.nchunk;
+    if (ns_req > 0 && ns_req < ns) ns = ns_req;
+    if (ns < 1) return LQ_E_SHAPE;
+    a.ns = ns;
+    size_t ring = size_t(ns) * S::STAGE_BYTES;
+    if (ring < size_t(S::RED_BYTES)) ring = S::RED_BYTES;
+    const size_t smem = ring + fixed;
+    if (smem > di.smem_optin) return LQ_E_SHAPE;
+
+    // weight boxes of 16 FR rows (CTAs holding FR fragments) and 16 (FR - 1) rows (the others), two segments a stage
+    CUtensorMap tw[2];
+    for (int m = 0; m < 2; ++m) {
+        const int rows = 16 * (m == 0 || FR == 1 ? FR : FR - 1);
+        const uint64_t dims[3] = {32, uint64_t(a.N), uint64_t(K) / 256};
+        const uint64_t str[2] = {uint64_t(K) / 2, 128};
+        const uint32_t box[3] = {32, uint32_t(rows), 2};
+        const int rc =
+            make_tmap(&tw[m], CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, w, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
+    a.x = x;
+    const int kg = a.kg;
+    const uintptr_t sb_addr = reinterpret_cast<uintptr_t>(a.s) | reinterpret_cast<uintptr_t>(a.b);
+    a.sb_vec = (kg % 8 == 0 && sb_addr % 16 == 0) ? 16 : (kg % 4 == 0 && sb_addr % 8 == 0) ? 8 : 4;
+
+    auto kern = qmvg_kernel<T, MT, FR>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return LQ_E_CUDA;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(nctas, 1, 1);
+    cfg.blockDim = dim3(QG_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, tw[0], tw[1], a);
+    return e == cudaSuccess ? LQ_OK : LQ_E_CUDA;
+}
+
+template <typename T, int MT>
+static int qmvg_dispatch_fr(int FR, const void* x, const uint32_t* w, const QgArgs& a, int ns, int nctas,
+                            cudaStream_t st) {
+    switch (FR) {
+        case 1: return qmvg_launch_t<T, MT, 1>(x, w, a, ns, nctas, st);
+        case 2: return qmvg_launch_t<T, MT, 2>(x, w, a, ns, nctas, st);
+        case 3: return qmvg_launch_t<T, MT, 3>(x, w, a, ns, nctas, st);
+        case 4: return qmvg_launch_t<T, MT, 4>(x, w, a, ns, nctas, st);
+        default: return LQ_E_SHAPE;
+    }
+}
+
+bool qmvg_shape_ok(int M, int K, int bits) { return bits == 4 && M >= 1 && M <= 16 && K >= 256 && K % 256 == 0; }
+
+// p = {FR (max fragments a CTA, 0 = spread over every SM), NS (stages, 0 = choose)}.
+int qmvg_run(const void* x, const uint32_t* w, const void* s, const void* b, int nout, void* const* outs,
+             const int* seg_end, const int* ldo, int M, int N, int K, int dtype, const int* p, cudaStream_t st) {
+    if (!qmvg_shape_ok(M, K, 4) || N < 1) return LQ_E_SHAPE;
+    QgArgs a = {};
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.kg = K / 64;
+    a.nchunk = (K + 511) / 512;
+    a.nfrag = (N + 15) / 16;
+    a.s = s;
+    a.b = b;
+    for (int i = 0; i < nout; ++i) {
+        a.out[i] = outs[i];
+        a.seg_end[i] = seg_end[i];
+        a.ldo[i] = ldo[i];
+    }
+    a.nseg_out = nout;
+    const int sms = device_info().sm_count;
+    const int fr_req = p ? p[0] : 0;
+    const int ns = p ? p[1] : 0;
+    if (fr_req < 0 || fr_req > QG_MAX_FR) return LQ_E_ARG;
+    // CTAs: at most fr fragments each; the library's choice spreads them over every SM. Then every CTA holds FR or
+    // FR - 1 fragments with FR = ceil(nfrag / nctas), the two weight-box heights the kernel is given.
+    int fr = fr_req;
+    if (fr == 0) {
+        fr = (a.nfrag + sms - 1) / sms;
+        if (fr > QG_MAX_FR) fr = QG_MAX_FR;
+    }
+    int nctas = (a.nfrag + fr - 1) / fr;
+    if (fr_req == 0 && nctas < sms) nctas = a.nfrag < sms ? a.nfrag : sms;
+    const int FR = (a.nfrag + nctas - 1) / nctas;
+    const bool bf16 = dtype == LQ_BF16;
+    if (M <= 8)
+        return bf16 ? qmvg_dispatch_fr<__nv_bfloat16, 1>(FR, x, w, a, ns, nctas, st)
+                    : qmvg_dispatch_fr<__half, 1>(FR, x, w, a, ns, nctas, st);
+    return bf16 ? qmvg_dispatch_fr<__nv_bfloat16, 2>(FR, x, w, a, ns, nctas, st)
+                : qmvg_dispatch_fr<__half, 2>(FR, x, w, a, ns, nctas, st);
+}
+
+}  // namespace lq

@@ -11,6 +11,8 @@ every path is a hand-written sm_100a kernel of liblq.so:
 
 * ``("qmv", MT, WK, KS, NS)`` -- decode family (TMA-staged packed weights, register dequant into
   mma.sync fragments, cluster split-K), any M (weights streamed once per 64 rows);
+* ``("qmvg", FR, NS)`` -- dense 4-bit decode for M <= 16: each warp takes one 64-wide group of every stage for
+  all of its CTA's 16-row fragments (x loaded once per group), fragments spread over every SM;
 * ``("tcv", NTOK, KS, WS[, PERSISTENT])`` -- the tensor-core family with weights dequantized into tensor
   memory as the MMA's A operand and tokens as its N side (16..256 columns); PERSISTENT = 1 runs one CTA
   per SM over all tiles (K % 256 == 0 at 4 bits);
@@ -89,7 +91,7 @@ def dequantize(wq: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, gro
 
 # ---- matmul ------------------------------------------------------------------------------------
 
-_FAMILY = {"auto": _lib.FAM_AUTO, "qmv": _lib.FAM_QMV, "tc": _lib.FAM_TC, "tcv": _lib.FAM_TCV}
+_FAMILY = {"auto": _lib.FAM_AUTO, "qmv": _lib.FAM_QMV, "tc": _lib.FAM_TC, "tcv": _lib.FAM_TCV, "qmvg": _lib.FAM_QMVG}
 
 
 def _cfg(choice: Optional[Sequence]):
@@ -178,7 +180,7 @@ def launch(choice: Sequence, M: int, K: int, N: int, dtype: torch.dtype, bits: i
 
 
 _FAMILY_NAME = {v: k for k, v in _FAMILY.items()}
-_NPARAM = {"qmv": 4, "tcv": 4, "tc": 1}
+_NPARAM = {"qmv": 4, "tcv": 4, "tc": 1, "qmvg": 2}
 
 
 def candidates(M: int, K: int, N: int, bits: int = 4, dtype: torch.dtype = torch.bfloat16) -> list:
