@@ -585,6 +585,7 @@ def run_gpu(args):
 CASES = {
     "qkv16": "fused QKV decode, x bf16 [16,2560] . 4-bit [6144,2560]^T, 8 distinct layers (72 MB)",
     "qkv16_l2": "fused QKV decode over 24 layers (218 MB > L2), for DRAM figures",
+    "qkv1_l2": "fused QKV decode at M=1 (the group-per-warp qmvg kernel) over 24 layers (218 MB > L2)",
     "mlp64": "8-bit MLP gate||up + SiLU.mul and down at M=64, 4 layers",
     "tc": "prefill GEMM x bf16 [1024,4096] . 4-bit [7168,4096]^T",
     "moe16": "MoE layer, 64 experts top-4, D 2048, I 768, M=16",
@@ -604,10 +605,10 @@ def run_case(name):
     dev = torch.device("cuda", 0)
     gen = torch.Generator(device=dev)
     gen.manual_seed(0)
-    if name in ("qkv16", "qkv16_l2"):
+    if name in ("qkv16", "qkv16_l2", "qkv1_l2"):
         L = 8 if name == "qkv16" else 24
         Ws = [make_layer(torch, HEAD_N, HEAD_K, 4, torch.bfloat16, gen, dev) for _ in range(L)]
-        x = torch.randn((16, HEAD_K), generator=gen, device=dev).to(torch.bfloat16)
+        x = torch.randn((1 if name == "qkv1_l2" else 16, HEAD_K), generator=gen, device=dev).to(torch.bfloat16)
         for _ in range(3):
             for w, s, b in Ws:
                 kernels.qmm_split(x, w, s, b, HEAD_WIDTHS)

@@ -35,7 +35,8 @@ extern "C" {
 #define LQ_F32 2
 
 /* Kernel families, the analogue of the reference's tuning choices (locals/kernels.py:136-144). */
-#define LQ_FAM_AUTO 0   /* pick by shape: TC from 65 rows; TCV for 33-64 rows or >= 24 MB of weights from 9 rows; else QMV */
+#define LQ_FAM_AUTO 0   /* pick by shape: TC from 65 rows; TCV for 33-64 rows or >= 24 MB of weights from 9 rows;
+                           QMVG for 1-4 rows of a 4-bit matrix (K % 256 == 0); else QMV */
 #define LQ_FAM_QMV 1    /* decode: TMA-staged packed weights, register dequant, mma.sync; p = {MT, WK, KS, NS} */
 #define LQ_FAM_TC 2     /* prefill: dequant tiles into shared memory, tcgen05.mma into TMEM */
 #define LQ_FAM_TCV 3    /* tcgen05 with weights dequantized into TMEM (A operand), tokens as N;

@@ -10,6 +10,10 @@
 //    stage for ALL the CTA's fragments: it loads and permutes its x fragments once (two 16-byte loads and 8 prmt a
 //    token tile) and reuses them for every fragment. The eight warps' partial sums are added through shared memory
 //    at the end (no global scratch, no atomics).
+//  * x never passes through shared memory: each consumer warp loads the 32 bytes a lane needs of its own group
+//    straight into registers (two 16-byte loads a token tile, one stage ahead of its use). Every CTA needs all of x
+//    (80 KB at 16 tokens, more than its share of the weights), and measured on B200 one producer warp feeds an SM at
+//    only ~20 GB/s, so x is spread over the 256 consumer lanes instead.
 //  * A lane reads 8 bytes (16 codes) of a row per group, so all four lanes of an MMA k-slice hold codes of the same
 //    group; codes are dequantized straight into m16n8k16 A fragments (magic exponent: 128 + q exact in bf16, 1024 + q
 //    in fp16; one subtract and one fma with the group's scale and bias -- the weight rounded once to the activation
@@ -17,11 +21,10 @@
 //    locals/qmv_frag.py:1-19); lane t's codes (p, p + 4) of word 2t + (s >> 1) meet x values 16t + 8(s >> 1) + p,
 //    + p + 4 of the same group, which is the permutation applied to x.
 //  * One producer warp: one TMA box a stage for the packed words of all the CTA's rows ([128-byte segment][16 nf rows]
-//    [2 segments], 128-byte swizzle, L2 evict-first), cp.async for x (only the M real token rows, written in the same
-//    swizzled layout) and for scales and biases (zero-filled past K and past N). The SM's TMA unit spends about the
-//    same time on a 4 KB box as on a 16 KB one (measured on B200), so the kernel issues as few boxes as it can: one a
-//    stage. The weight boxes of the first stages are issued before griddepcontrol.wait, so under programmatic
-//    dependent launch they overlap the previous kernel; only x waits.
+//    [2 segments], 128-byte swizzle, L2 evict-first; one box rather than one a fragment measured faster) and cp.async
+//    for scales and biases (zero-filled past K and past N). Nothing it loads comes from the previous kernel, so under
+//    programmatic dependent launch the whole ring fills while the previous kernel still runs; only the consumers'
+//    x loads wait for the grid dependency.
 // Reference: the multi-row GEMV it replaces, locals/qmv_multi.py:16-248 and locals/qmv_frag.py:34-540, behind
 // kernels._launcher (locals/kernels.py:516-576).
 #include <cuda.h>
@@ -47,11 +50,10 @@ struct QgShape {
     static constexpr int MTOK = 8 * MT;                  // token slots
     static constexpr int W_FRAG = 16 * 256;              // one 16-row fragment: 256 bytes (512 codes) a row
     static constexpr int W_BYTES = FR * W_FRAG;
-    static constexpr int X_BYTES = 8 * MTOK * 128;       // 8 groups x MTOK tokens x 64 values (rows past M unused)
     static constexpr int SB_BYTES = FR * 16 * 16;        // scales (or biases): rows x 8 groups x 2 bytes
-    static constexpr int STAGE_BYTES = (W_BYTES + X_BYTES + 2 * SB_BYTES + 1023) / 1024 * 1024;
+    static constexpr int STAGE_BYTES = (W_BYTES + 2 * SB_BYTES + 1023) / 1024 * 1024;
     static constexpr int RED_BYTES = QG_CW * MTOK * FR * 16 * 4;  // the warps' partial sums
-    static_assert(W_FRAG % 1024 == 0 && X_BYTES % 1024 == 0, "1 KB alignment of swizzled tiles");
+    static_assert(W_FRAG % 1024 == 0, "1 KB alignment of swizzled tiles");
 };
 
 struct QgArgs {
@@ -161,7 +163,7 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
                 mbar_arrive_expect_tx(&full[s], nf * S::W_FRAG);
                 tma_load_3d(st, tm_w, &full[s], 0, row0, 2 * c, pol_w);
             }
-            const uint32_t sdst = smem_base + s * S::STAGE_BYTES + S::W_BYTES + S::X_BYTES;
+            const uint32_t sdst = smem_base + s * S::STAGE_BYTES + S::W_BYTES;
             const uint8_t* sbase = reinterpret_cast<const uint8_t*>(a.s);
             const uint8_t* bbase = reinterpret_cast<const uint8_t*>(a.b);
             for (int r = lane; r < nf * 16; r += 32) {
@@ -176,24 +178,9 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
                 }
             }
         };
-        // x values of stage c for the real token rows: 16-byte pieces, consecutive lanes along K (coalesced), written
-        // to [group][token][128 bytes] with piece p of token row r at p ^ (r & 7); zero past K
-        const uint8_t* xg = reinterpret_cast<const uint8_t*>(a.x);
-        auto load_x = [&](int c, int s) {
-            const uint32_t xdst = smem_base + s * S::STAGE_BYTES + S::W_BYTES;
-            for (int e = lane; e < 64 * mv; e += 32) {
-                const int tok = e >> 6, j = (e >> 3) & 7, p = e & 7;
-                const int k = (8 * c + j) * 64 + 8 * p;
-                const bool valid = k < a.K;
-                cp_async(xdst + j * (S::MTOK * 128) + tok * 128 + ((p ^ (tok & 7)) << 4),
-                         xg + (valid ? (size_t(tok) * a.K + k) * 2 : 0), 16, valid);
-            }
-        };
         const int pre = total < ns ? total : ns;
-        for (int i = 0; i < pre; ++i) load_weights(i, i);
-        grid_dep_wait();  // x may be the previous kernel's output
-        for (int i = 0; i < pre; ++i) {
-            load_x(i, i);
+        for (int i = 0; i < pre; ++i) {  // (weights and scales only: nothing here waits for the previous kernel)
+            load_weights(i, i);
             cp_async_arrive(&full[i]);
         }
         if (lane == 0) grid_dep_launch();
@@ -202,7 +189,6 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
             ok = mbar_wait(&empty[s], ((i / ns) - 1) & 1);
             if (!ok) break;
             load_weights(i, s);
-            load_x(i, s);
             cp_async_arrive(&full[s]);
         }
         __syncwarp();
@@ -210,7 +196,7 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
     }
 
     // ------------------------------ consumer warps ------------------------------
-    grid_dep_wait();  // (before any output store of this kernel)
+    grid_dep_wait();  // x may be the previous kernel's output (and before any output store of this kernel)
     const int g = lane >> 2, t = lane & 3;
     const uint32_t smem_base = smem_u32(smem);
     float acc[FR][MT][4];
@@ -224,20 +210,37 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
     // this lane's 8 bytes of a row inside group w of a stage (128-byte swizzle: 16-byte chunk c of row r sits at
     // c ^ (r & 7)); the stage's box is [segment][16 nf rows][128 bytes], fragment f's rows at 2048 f of each segment
     const uint32_t w_off = (warp >> 2) * (nf * 2048) + g * 128 + (((2 * (warp & 3) + (t >> 1)) ^ g) << 4) + 8 * (t & 1);
-    const uint32_t x_off = warp * (S::MTOK * 128) + g * 128;
-    const uint32_t x_c0 = ((2 * t) ^ g) << 4, x_c1 = ((2 * t + 1) ^ g) << 4;
+    // x of stage i's group for this lane: values 16t .. 16t + 15 of tokens g + 8 mt (zero past M and past K)
+    const uint8_t* xg = reinterpret_cast<const uint8_t*>(a.x);
+    auto fetch_x = [&](int i, uint4 (&u)[MT][2]) {
+        const int gi = 8 * i + warp;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+            const int tok = 8 * mt + g;
+            if (tok < a.M && gi < a.kg) {
+                const uint4* p = reinterpret_cast<const uint4*>(xg + (size_t(tok) * a.K + gi * 64 + 16 * t) * 2);
+                u[mt][0] = p[0];
+                u[mt][1] = p[1];
+            } else {
+                u[mt][0] = make_uint4(0u, 0u, 0u, 0u);
+                u[mt][1] = make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
+    };
+    uint4 xc[MT][2], xn[MT][2];
+    fetch_x(0, xc);
 
     for (int i = 0; i < total; ++i) {
         const int s = i % ns;
+        if (i + 1 < total) fetch_x(i + 1, xn);  // one stage ahead of its use
         if (ok) ok = mbar_wait(&full[s], (i / ns) & 1);
         if (ok && 8 * i + warp < a.kg) {
             const uint32_t st = smem_base + s * S::STAGE_BYTES;
-            // x fragments of group w: values 16t .. 16t + 15 of tokens g (+ 8 mt), permuted to the code order
+            // x fragments of group w permuted to the code order
             uint32_t xb[MT][4][2];
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) {
-                const uint32_t xr = st + S::W_BYTES + x_off + mt * 8 * 128;
-                const uint4 u0 = lds128(xr + x_c0), u1 = lds128(xr + x_c1);
+                const uint4 u0 = xc[mt][0], u1 = xc[mt][1];
                 xb[mt][0][0] = prmt(u0.x, u0.z, 0x5410);
                 xb[mt][0][1] = prmt(u0.x, u0.z, 0x7632);
                 xb[mt][1][0] = prmt(u0.y, u0.w, 0x5410);
@@ -247,7 +250,7 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
                 xb[mt][3][0] = prmt(u1.y, u1.w, 0x5410);
                 xb[mt][3][1] = prmt(u1.y, u1.w, 0x7632);
             }
-            const uint32_t sb = st + S::W_BYTES + S::X_BYTES + 2 * warp;
+            const uint32_t sb = st + S::W_BYTES + 2 * warp;
 #pragma unroll
             for (int f = 0; f < FR; ++f) {
                 if (f < nf) {
@@ -278,6 +281,11 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+            xc[mt][0] = xn[mt][0];
+            xc[mt][1] = xn[mt][1];
+        }
     }
 
     // ---- the eight warps' partial sums, added through shared memory (the ring is free: every stage was consumed) ----
