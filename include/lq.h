@@ -58,6 +58,19 @@ typedef struct lq_cfg {
 int lq_qmm(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int M, int N, int K,
            int bits, int group_size, int dtype, const lq_cfg* cfg, void* stream);
 
+/* Large-M quantized matmul the way the reference's dense prefill path computes it (locals/kernels.py:999-1025,
+ * `_dense_matmul`: mx.dequantize into a temporary, then x @ w.T; chosen there for N x K <= 2^27 weights,
+ * kernels.py:858-866): the weights are dequantized once into `workspace` (N x K in dtype, rounded once to dtype as
+ * mx.dequantize rounds them) and y (M, N) = x . w^T runs as a dense tcgen05 GEMM (fp32 accumulation).
+ * workspace_bytes >= lq_qmm_dense_workspace(N, K); workspace and y 16-byte aligned; K % 64 == 0; bits 4 or 8.
+ * cfg: NULL, or family LQ_FAM_TC with p[0] = the N tile (128, 224 or 256; 0 = choose). */
+int lq_qmm_dense(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int M, int N, int K,
+                 int bits, int group_size, int dtype, void* workspace, size_t workspace_bytes, const lq_cfg* cfg,
+                 void* stream);
+
+/* Bytes of workspace lq_qmm_dense needs: N * K * 2. Host-only. */
+size_t lq_qmm_dense_workspace(int N, int K);
+
 /* Fused projection with its output split along N (the fused q/k/v projection): columns
  * [0, widths[0]) of x . dequant(w)^T go to outs[0] (M, widths[0]), the next widths[1] to outs[1],
  * ... (nout <= 3, sum of widths = N). Replaces fuse._concat_quantized + FusedAttention's reshape

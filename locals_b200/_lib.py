@@ -43,6 +43,9 @@ SIGNATURES = {
     "lq_kv_attend": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, ctypes.c_float, _i, _i, _i, _i, _i, _i, _vp,
                       ctypes.c_size_t, _vp, _vp], _i),
     "lq_kv_attend_workspace": ([_i, _i, _i, _i], ctypes.c_size_t),
+    "lq_qmm_dense": ([_vp, _u32p, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, ctypes.c_size_t, ctypes.POINTER(Cfg), _vp],
+                     _i),
+    "lq_qmm_dense_workspace": ([_i, _i], ctypes.c_size_t),
     "lq_kv_attend_noalloc": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, ctypes.c_float, _i, _i, _i, _i, _i, _i,
                               _vp, _vp], _i),
     "lq_supported": ([_i, _i, _i, _i, _i, _i, _i], _i),

@@ -43,6 +43,10 @@ int tcvp_run_grouped(const void* xs, int P, const QmvMats& mats, int nmat, int N
                      const int32_t* starts, const int32_t* experts, const int32_t* nseg, int E, int bits, int dtype,
                      int ntok, cudaStream_t st);
 bool norm_shape_ok(int D);
+size_t qmm_dense_workspace_bytes(int N, int K);
+bool qmm_dense_shape_ok(int M, int N, int K, int bits);
+int qmm_dense_run(const void* x, const uint32_t* w, const void* s, const void* b, void* y, int M, int N, int K,
+                  int bits, int dtype, void* workspace, const int* p, cudaStream_t st);
 bool qmvg_shape_ok(int M, int K, int bits);
 int qmvg_run(const void* x, const uint32_t* w, const void* s, const void* b, int nout, void* const* outs,
              const int* seg_end, const int* ldo, int M, int N, int K, int dtype, const int* p, cudaStream_t st);
@@ -377,6 +381,28 @@ int lq_add_rms_norm(const void* x, const void* r, const void* w, void* h, void* 
     int rc = check_device();
     if (rc) return rc;
     return finish(add_rms_run(x, r, w, h, n, rows, D, eps, dtype, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+size_t lq_qmm_dense_workspace(int N, int K) {
+    if (N < 1 || K < 1) return 0;
+    return qmm_dense_workspace_bytes(N, K);
+}
+
+int lq_qmm_dense(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int M, int N, int K,
+                 int bits, int group_size, int dtype, void* workspace, size_t workspace_bytes, const lq_cfg* cfg,
+                 void* stream) {
+    int rc = check_common(x, w, scales, biases, M, N, K, bits, group_size, dtype);
+    if (rc) return rc;
+    if (!y || !workspace) return LQ_E_ARG;
+    if (!qmm_dense_shape_ok(M, N, K, bits)) return LQ_E_SHAPE;
+    if (workspace_bytes < qmm_dense_workspace_bytes(N, K)) return LQ_E_ARG;
+    if (!aligned(workspace, 16) || !aligned(y, 16) || (bits == 4 && (!aligned(scales, 2) || !aligned(biases, 2))))
+        return LQ_E_ALIGN;
+    rc = check_device();
+    if (rc) return rc;
+    return finish(qmm_dense_run(x, w, scales, biases, y, M, N, K, bits, dtype, workspace,
+                                (cfg && cfg->family == LQ_FAM_TC) ? cfg->p : nullptr,
+                                reinterpret_cast<cudaStream_t>(stream)));
 }
 
 size_t lq_kv_attend_workspace(int B, int H, int KVH, int n) {

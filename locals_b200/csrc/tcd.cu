@@ -1,0 +1,306 @@
+// Prefill as the reference's dense path: the weights dequantized once into the activation dtype, then a dense
+// GEMM on the 5th-generation tensor cores (locals/kernels.py:999-1025, `_dense_matmul`: mx.dequantize into a
+// temporary, then x @ w.T; used by the reference for N x K <= 2^27 weights, kernels.py:858-866).
+//
+// Why a second prefill form. The fused tc kernel dequantizes each weight tile inside every CTA that uses it, so at
+// M = 2048 each weight is dequantized 16 times (once per 128-row token tile), and the dequant warps, not the tensor
+// cores, bound it. Dequantizing once costs one HBM pass (read the 4-bit words, write the 16-bit weights: ~150 MB at
+// config 5), after which the GEMM streams both operands by TMA and only the tensor pipe works.
+//
+// dequant4_kernel: one thread per 16 bytes of packed words (32 codes, half a group): one 16-byte load, per word one
+//   shift, one lop3 with the 16-bit float magic exponent, one subtract and one fma per code pair (the weight
+//   rounded once to the activation dtype, as mx.dequantize rounds it), four 16-byte stores in K order.
+// tcd_kernel: one CTA per 128 x BN output tile, six warps: warp 4 streams the x tile (128 x 64) and the weight tile
+//   (BN x 64), both 128-byte swizzled K-major (the UMMA canonical layout), into a ring by TMA; warp 5 allocates BN
+//   TMEM columns and issues tcgen05.mma (kind::f16, M = 128, N = BN, K = 16, fp32 accumulator) from one lane,
+//   committing each slot back to the producer; warps 0-3 read the accumulator with tcgen05.ld (warp w: TMEM lanes
+//   32w ..) and store rounded rows. Every mbarrier wait is bounded; TMEM is always freed.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <type_traits>
+
+#include "lq_host.h"
+#include "lq_ptx.cuh"
+
+namespace lq {
+
+// ---- dequantize (4-bit, group 64) -----------------------------------------------------------------
+
+template <typename T>
+__global__ void __launch_bounds__(256) dequant4_kernel(const uint4* __restrict__ wq, const uint16_t* __restrict__ s,
+                                                       const uint16_t* __restrict__ b, int64_t n_units, int K,
+                                                       uint4* __restrict__ out) {
+    using TR = F16Traits<T>;
+    grid_dep_wait();
+    const int units_row = K / 32;  // 16-byte units (32 codes) a row
+    for (int64_t u = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; u < n_units; u += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t row = u / units_row;
+        const int piece = int(u - row * units_row);
+        const size_t g = size_t(row) * (K / 64) + (piece >> 1);
+        const uint32_t sv = s[g], bv = b[g];
+        const uint32_t s2 = prmt(sv, sv, 0x1010), b2 = prmt(bv, bv, 0x1010);
+        const uint4 w4 = wq[u];
+        const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
+        uint4* dst = out + u * 4;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            uint32_t p[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)  // codes (e, e + 4) of the word
+                p[e] = TR::sub_magic_fma(lop3_and_or(ws[c] >> (4 * e), 0x000F000Fu, TR::kMagic2), s2, b2);
+            dst[c] = make_uint4(prmt(p[0], p[1], 0x5410), prmt(p[2], p[3], 0x5410), prmt(p[0], p[1], 0x7632),
+                                prmt(p[2], p[3], 0x7632));  // K order (0,1) (2,3) (4,5) (6,7)
+        }
+    }
+    grid_dep_launch();
+}
+
+// ---- dense GEMM ---------------------------------------------------------------------------------
+
+constexpr int TCD_BM = 128;
+constexpr int TCD_BK = 64;
+constexpr int TCD_THREADS = 192;
+constexpr int TCD_MAX_STAGES = 6;
+
+template <int BN>
+struct TcdShape {
+    static constexpr int A_BYTES = TCD_BM * TCD_BK * 2;  // 16 KB
+    static constexpr int B_BYTES = BN * TCD_BK * 2;
+    static constexpr int STAGE = A_BYTES + B_BYTES;
+    static constexpr int FIT = (225 * 1024) / STAGE;
+    static constexpr int NS = FIT < TCD_MAX_STAGES ? FIT : TCD_MAX_STAGES;
+    static constexpr int TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+    static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "1 KB alignment of swizzled tiles");
+    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
+};
+
+struct TcdArgs {
+    int M, N, K, nk;
+    void* y;
+};
+
+template <typename T, int BN>
+__global__ void __launch_bounds__(TCD_THREADS, 1)
+    tcd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w, const TcdArgs a) {
+    using S = TcdShape<BN>;
+    using TR = F16Traits<T>;
+    constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::NS * S::STAGE);
+    uint64_t* empty = full + S::NS;
+    uint64_t* acc_full = empty + S::NS;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // token tiles vary fastest: the CTAs of one wave share their weight tiles (read once from DRAM, then from L2)
+    const int m0 = blockIdx.x * TCD_BM, n0 = blockIdx.y * BN;
+    const int nk = a.nk;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S::NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(acc_full, 1);
+        fence_barrier_init();
+    }
+    if (warp == 5) {
+        tmem_alloc(tmem_slot, S::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool ok = true;
+
+    if (warp == 4) {
+        // ------------------------------ producer ------------------------------
+        if (lane == 0) {
+            prefetch_tmap(&tm_x);
+            prefetch_tmap(&tm_w);
+            const uint64_t pol_x = policy_evict_last();
+            const uint64_t pol_w = policy_evict_last();
+            grid_dep_wait();  // x and the dequantized weights come from earlier kernels
+            for (int kb = 0; kb < nk; ++kb) {
+                const int s = kb % S::NS;
+                if (kb >= S::NS && !mbar_wait(&empty[s], ((kb / S::NS) - 1) & 1)) break;
+                uint8_t* st = smem + s * S::STAGE;
+                mbar_arrive_expect_tx(&full[s], S::STAGE);
+                tma_load_2d(st, &tm_x, &full[s], kb * TCD_BK, m0, pol_x);
+                tma_load_2d(st + S::A_BYTES, &tm_w, &full[s], kb * TCD_BK, n0, pol_w);
+            }
+            grid_dep_launch();
+        }
+        __syncwarp();
+    } else if (warp == 5) {
+        // ------------------------------ MMA issuer ------------------------------
+        constexpr uint32_t idesc = umma_idesc_f16(kBF16 ? 1 : 0, TCD_BM, BN);
+        for (int kb = 0; kb < nk && ok; ++kb) {
+            const int s = kb % S::NS;
+            ok = mbar_wait(&full[s], (kb / S::NS) & 1);
+            if (!ok) break;
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t a_base = smem_u32(smem + s * S::STAGE);
+                const uint32_t b_base = a_base + S::A_BYTES;
+#pragma unroll
+                for (int k = 0; k < TCD_BK / 16; ++k)
+                    tc_mma_f16(tmem, umma_desc_sw128(a_base + k * 32), umma_desc_sw128(b_base + k * 32), idesc,
+                               (kb > 0 || k > 0) ? 1u : 0u);
+                tc_commit(&empty[s]);
+            }
+            __syncwarp();
+        }
+        if (lane == 0) tc_commit(acc_full);  // (also on an error path: completes once issued MMAs finish)
+        __syncwarp();
+    } else {
+        // ------------------------------ epilogue warps 0-3 ------------------------------
+        ok = mbar_wait(acc_full, 0);
+        tc_fence_after();
+        const int m = m0 + 32 * warp + lane;
+        T* yrow = reinterpret_cast<T*>(a.y) + size_t(m) * a.N;
+        const bool vec = (a.N & 7) == 0;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem + (uint32_t(32 * warp) << 16) + uint32_t(c0), r);
+            tmem_wait_ld();
+            if (!ok || m >= a.M) continue;
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                const int nn = n0 + c0 + 8 * v;
+                if (c0 + 8 * v >= BN || nn >= a.N) break;
+                uint32_t o[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    o[q] = TR::pack2(__uint_as_float(r[8 * v + 2 * q + 1]), __uint_as_float(r[8 * v + 2 * q]));
+                if (vec && nn + 8 <= a.N) {
+                    *reinterpret_cast<uint4*>(yrow + nn) = make_uint4(o[0], o[1], o[2], o[3]);
+                } else {
+                    for (int q = 0; q < 8; ++q)
+                        if (nn + q < a.N) {
+                            const uint32_t word = o[q >> 1];
+                            reinterpret_cast<uint16_t*>(yrow)[nn + q] =
+                                (q & 1) ? uint16_t(word >> 16) : uint16_t(word & 0xFFFF);
+                        }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tmem, S::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// host side
+// ------------------------------------------------------------------------------------------------
+
+static int pdl_launch(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, func, args) == cudaSuccess ? LQ_OK : LQ_E_CUDA;
+}
+
+template <typename T>
+static int dequant4_launch(const uint32_t* w, const void* s, const void* b, int N, int K, void* out, cudaStream_t st) {
+    int64_t n_units = int64_t(N) * (K / 32);
+    const int threads = 256;
+    int64_t blocks = (n_units + threads - 1) / threads;
+    const int64_t cap = int64_t(device_info().sm_count) * 8;
+    if (blocks > cap) blocks = cap;
+    const uint4* wq = reinterpret_cast<const uint4*>(w);
+    const uint16_t* sp = static_cast<const uint16_t*>(s);
+    const uint16_t* bp = static_cast<const uint16_t*>(b);
+    int K_ = K;
+    uint4* o = static_cast<uint4*>(out);
+    void* args[] = {&wq, &sp, &bp, &n_units, &K_, &o};
+    return pdl_launch(reinterpret_cast<const void*>(dequant4_kernel<T>), dim3(unsigned(blocks)), dim3(threads), 0, st,
+                      args);
+}
+
+template <typename T, int BN>
+static int tcd_launch_t(const void* x, const void* wd, void* y, int M, int N, int K, cudaStream_t st) {
+    using S = TcdShape<BN>;
+    TcdArgs a;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.nk = K / TCD_BK;
+    a.y = y;
+    CUtensorMap tx, tw;
+    {
+        const uint64_t dims[2] = {uint64_t(K), uint64_t(M)};
+        const uint64_t str[1] = {uint64_t(K) * 2};
+        const uint32_t box[2] = {TCD_BK, TCD_BM};
+        int rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, x, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
+    {
+        const uint64_t dims[2] = {uint64_t(K), uint64_t(N)};
+        const uint64_t str[1] = {uint64_t(K) * 2};
+        const uint32_t box[2] = {TCD_BK, uint32_t(BN)};
+        int rc = make_tmap(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, wd, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
+    const size_t smem = 1024 + size_t(S::NS) * S::STAGE + (2 * S::NS + 2) * 8 + 64;
+    if (smem > device_info().smem_optin) return LQ_E_SHAPE;
+    auto kern = tcd_kernel<T, BN>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return LQ_E_CUDA;
+    void* args[] = {&tx, &tw, &a};
+    return pdl_launch(reinterpret_cast<const void*>(kern), dim3((M + TCD_BM - 1) / TCD_BM, (N + BN - 1) / BN, 1),
+                      dim3(TCD_THREADS), smem, st, args);
+}
+
+size_t qmm_dense_workspace_bytes(int N, int K) { return size_t(N) * size_t(K) * 2; }
+
+bool qmm_dense_shape_ok(int M, int N, int K, int bits) {
+    return M >= 1 && N >= 16 && K >= 64 && K % 64 == 0 && (bits == 4 || bits == 8);
+}
+
+int dequantize_run(const uint32_t* wq, const void* s, const void* b, int N, int K, int bits, int group, int dt,
+                   void* out, cudaStream_t st);
+
+// p = {BN (0 = 224 when that divides N, else 256)}. workspace: N x K weights in the activation dtype.
+int qmm_dense_run(const void* x, const uint32_t* w, const void* s, const void* b, void* y, int M, int N, int K,
+                  int bits, int dtype, void* workspace, const int* p, cudaStream_t st) {
+    const bool bf16 = dtype == LQ_BF16;
+    int rc;
+    if (bits == 4)
+        rc = bf16 ? dequant4_launch<__nv_bfloat16>(w, s, b, N, K, workspace, st)
+                  : dequant4_launch<__half>(w, s, b, N, K, workspace, st);
+    else
+        rc = dequantize_run(w, s, b, N, K, bits, 64, dtype, workspace, st);
+    if (rc) return rc;
+    int bn = p ? p[0] : 0;
+    if (bn == 0) bn = (N % 224 == 0) ? 224 : 256;
+#define LQ_TCD_CASE(BN_) \
+    if (bn == BN_)       \
+        return bf16 ? tcd_launch_t<__nv_bfloat16, BN_>(x, workspace, y, M, N, K, st) : tcd_launch_t<__half, BN_>(x, workspace, y, M, N, K, st);
+    LQ_TCD_CASE(256)
+    LQ_TCD_CASE(224)
+    LQ_TCD_CASE(128)
+#undef LQ_TCD_CASE
+    return LQ_E_ARG;
+}
+
+}  // namespace lq

@@ -101,11 +101,31 @@ def _cfg(choice: Optional[Sequence]):
     return _lib.cfg(fam, *choice[1:])
 
 
+# The reference's dense prefill rule (locals/kernels.py:854-866): dequantize + dense GEMM for weights of at most
+# DENSE_MAX values. Here from DENSE_M rows: below that the fused kernels win (the dequantize pass is a fixed
+# ~25 us on a 14336 x 4096 matrix; measured on B200).
+DENSE_MAX = 1 << 27
+DENSE_M = 512
+
+
+def dense_default(M: int, N: int, K: int, bits: int, group_size: int = 64) -> bool:
+    return M >= DENSE_M and N * K <= DENSE_MAX and group_size == 64 and bits in (4, 8) and K % 64 == 0 and N >= 16
+
+
+def _qmm_dense(x2: torch.Tensor, w, scales, biases, y, M, N, K, bits, group_size, bn: int = 0) -> None:
+    nbytes = int(_lib.lib().lq_qmm_dense_workspace(N, K))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=x2.device)  # the dequantized weights (a temporary, as MLX's)
+    cfg = _lib.cfg(_lib.FAM_TC, bn) if bn else None
+    call("lq_qmm_dense", x2.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(), y.data_ptr(), M, N, K,
+         bits, group_size, dtype_code(x2.dtype), ws.data_ptr(), nbytes, cfg, _stream())
+
+
 def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
                      transpose: bool = True, group_size: int = 64, bits: int = 4,
                      choice: Optional[Sequence] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """y = x . dequant(w)^T (mx.quantized_matmul(x, w, scales, biases, transpose=True, group_size, bits))
-    for x (..., K) fp16/bf16. ``choice`` = ("qmv", MT, WK, KS, NS) / ("tc", ...) / None (auto)."""
+    for x (..., K) fp16/bf16. ``choice`` = ("qmv", MT, WK, KS, NS) / ("tc", ...) / ("dense"[, BN]) / None (auto:
+    from DENSE_M rows, the reference's dequantize + dense GEMM path, locals/kernels.py:999-1025)."""
     if not transpose:
         raise NotImplementedError("only transpose=True (the layout of every reference call site)")
     shape = x.shape
@@ -119,6 +139,9 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, bia
     if scales.dtype != x.dtype or biases.dtype != x.dtype:
         raise TypeError("scales and biases must have the activations' dtype")
     y = out if out is not None else torch.empty((M, N), dtype=x.dtype, device=x.device)
+    if (choice is not None and choice[0] == "dense") or (choice is None and dense_default(M, N, K, bits, group_size)):
+        _qmm_dense(x2, w, scales, biases, y, M, N, K, bits, group_size, int(choice[1]) if choice and len(choice) > 1 else 0)
+        return y.reshape(*shape[:-1], N)
     call("lq_qmm", x2.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(), y.data_ptr(), M, N, K, bits,
          group_size, dtype_code(x.dtype), _cfg(choice), _stream())
     return y.reshape(*shape[:-1], N)
