@@ -10,11 +10,13 @@
 // dequant4_kernel: one thread per 16 bytes of packed words (32 codes, half a group): one 16-byte load, per word one
 //   shift, one lop3 with the 16-bit float magic exponent, one subtract and one fma per code pair (the weight
 //   rounded once to the activation dtype, as mx.dequantize rounds it), four 16-byte stores in K order.
-// tcd_kernel: one CTA per 128 x BN output tile, six warps: warp 4 streams the x tile (128 x 64) and the weight tile
-//   (BN x 64), both 128-byte swizzled K-major (the UMMA canonical layout), into a ring by TMA; warp 5 allocates BN
-//   TMEM columns and issues tcgen05.mma (kind::f16, M = 128, N = BN, K = 16, fp32 accumulator) from one lane,
-//   committing each slot back to the producer; warps 0-3 read the accumulator with tcgen05.ld (warp w: TMEM lanes
-//   32w ..) and store rounded rows. Every mbarrier wait is bounded; TMEM is always freed.
+// tcd_kernel: persistent, one CTA per SM walking 128 x BN output tiles (token tiles fastest), six warps: warp 4
+//   streams the x tile (128 x 64) and the weight tile (BN x 64), both 128-byte swizzled K-major (the UMMA canonical
+//   layout), into a ring by TMA, running ahead across tiles; warp 5 allocates two BN-column TMEM accumulators and
+//   issues tcgen05.mma (kind::f16, M = 128, N = BN, K = 16, fp32) from one lane, committing each slot back to the
+//   producer and each finished tile to the epilogue; warps 0-3 read a finished accumulator with tcgen05.ld (warp w:
+//   TMEM lanes 32w ..), store rounded rows and hand the accumulator back -- so a tile's epilogue runs under the next
+//   tile's MMAs. Every mbarrier wait is bounded; TMEM is always freed.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -73,13 +75,15 @@ struct TcdShape {
     static constexpr int STAGE = A_BYTES + B_BYTES;
     static constexpr int FIT = (225 * 1024) / STAGE;
     static constexpr int NS = FIT < TCD_MAX_STAGES ? FIT : TCD_MAX_STAGES;
-    static constexpr int TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+    static constexpr int ACC_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;  // one accumulator
+    static constexpr int TMEM_COLS = 2 * ACC_COLS;                                           // double-buffered
     static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "1 KB alignment of swizzled tiles");
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
 };
 
 struct TcdArgs {
     int M, N, K, nk;
+    int mt, ntiles;  // token tiles, all tiles
     void* y;
 };
 
@@ -94,20 +98,25 @@ __global__ void __launch_bounds__(TCD_THREADS, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::NS * S::STAGE);
     uint64_t* empty = full + S::NS;
-    uint64_t* acc_full = empty + S::NS;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+    uint64_t* acc_full = empty + S::NS;  // [2] the MMAs of a tile are done
+    uint64_t* acc_empty = acc_full + 2;  // [2] the epilogue has read the accumulator
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // token tiles vary fastest: the CTAs of one wave share their weight tiles (read once from DRAM, then from L2)
-    const int m0 = blockIdx.x * TCD_BM, n0 = blockIdx.y * BN;
     const int nk = a.nk;
+    // tiles of this CTA: blockIdx.x, blockIdx.x + gridDim.x, ...; token tiles vary fastest, so the CTAs working at
+    // one time share their weight tiles (read once from DRAM, then from L2)
+    const int my_tiles = a.ntiles > int(blockIdx.x) ? (a.ntiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x) : 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S::NS; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(acc_full, 1);
+        for (int j = 0; j < 2; ++j) {
+            mbar_init(&acc_full[j], 1);
+            mbar_init(&acc_empty[j], 4);  // lane 0 of each epilogue warp
+        }
         fence_barrier_init();
     }
     if (warp == 5) {
@@ -128,13 +137,18 @@ __global__ void __launch_bounds__(TCD_THREADS, 1)
             const uint64_t pol_x = policy_evict_last();
             const uint64_t pol_w = policy_evict_last();
             grid_dep_wait();  // x and the dequantized weights come from earlier kernels
-            for (int kb = 0; kb < nk; ++kb) {
-                const int s = kb % S::NS;
-                if (kb >= S::NS && !mbar_wait(&empty[s], ((kb / S::NS) - 1) & 1)) break;
-                uint8_t* st = smem + s * S::STAGE;
-                mbar_arrive_expect_tx(&full[s], S::STAGE);
-                tma_load_2d(st, &tm_x, &full[s], kb * TCD_BK, m0, pol_x);
-                tma_load_2d(st + S::A_BYTES, &tm_w, &full[s], kb * TCD_BK, n0, pol_w);
+            int it = 0;
+            for (int j = 0; j < my_tiles && ok; ++j) {
+                const int tile = int(blockIdx.x) + j * int(gridDim.x);
+                const int m0 = (tile % a.mt) * TCD_BM, n0 = (tile / a.mt) * BN;
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int s = it % S::NS;
+                    if (it >= S::NS && !(ok = mbar_wait(&empty[s], ((it / S::NS) - 1) & 1))) break;
+                    uint8_t* st = smem + s * S::STAGE;
+                    mbar_arrive_expect_tx(&full[s], S::STAGE);
+                    tma_load_2d(st, &tm_x, &full[s], kb * TCD_BK, m0, pol_x);
+                    tma_load_2d(st + S::A_BYTES, &tm_w, &full[s], kb * TCD_BK, n0, pol_w);
+                }
             }
             grid_dep_launch();
         }
@@ -142,56 +156,73 @@ __global__ void __launch_bounds__(TCD_THREADS, 1)
     } else if (warp == 5) {
         // ------------------------------ MMA issuer ------------------------------
         constexpr uint32_t idesc = umma_idesc_f16(kBF16 ? 1 : 0, TCD_BM, BN);
-        for (int kb = 0; kb < nk && ok; ++kb) {
-            const int s = kb % S::NS;
-            ok = mbar_wait(&full[s], (kb / S::NS) & 1);
+        int it = 0;
+        for (int j = 0; j < my_tiles && ok; ++j) {
+            const int buf = j & 1;
+            if (j >= 2) ok = mbar_wait(&acc_empty[buf], ((j >> 1) - 1) & 1);  // the epilogue read this accumulator
             if (!ok) break;
             tc_fence_after();
-            if (lane == 0) {
-                const uint32_t a_base = smem_u32(smem + s * S::STAGE);
-                const uint32_t b_base = a_base + S::A_BYTES;
+            const uint32_t acc = tmem + uint32_t(buf * S::ACC_COLS);
+            for (int kb = 0; kb < nk && ok; ++kb, ++it) {
+                const int s = it % S::NS;
+                ok = mbar_wait(&full[s], (it / S::NS) & 1);
+                if (!ok) break;
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t a_base = smem_u32(smem + s * S::STAGE);
+                    const uint32_t b_base = a_base + S::A_BYTES;
 #pragma unroll
-                for (int k = 0; k < TCD_BK / 16; ++k)
-                    tc_mma_f16(tmem, umma_desc_sw128(a_base + k * 32), umma_desc_sw128(b_base + k * 32), idesc,
-                               (kb > 0 || k > 0) ? 1u : 0u);
-                tc_commit(&empty[s]);
+                    for (int k = 0; k < TCD_BK / 16; ++k)
+                        tc_mma_f16(acc, umma_desc_sw128(a_base + k * 32), umma_desc_sw128(b_base + k * 32), idesc,
+                                   (kb > 0 || k > 0) ? 1u : 0u);
+                    tc_commit(&empty[s]);
+                }
+                __syncwarp();
             }
+            if (lane == 0) tc_commit(&acc_full[buf]);  // (also after an error: completes once issued MMAs finish)
             __syncwarp();
         }
-        if (lane == 0) tc_commit(acc_full);  // (also on an error path: completes once issued MMAs finish)
-        __syncwarp();
     } else {
         // ------------------------------ epilogue warps 0-3 ------------------------------
-        ok = mbar_wait(acc_full, 0);
-        tc_fence_after();
-        const int m = m0 + 32 * warp + lane;
-        T* yrow = reinterpret_cast<T*>(a.y) + size_t(m) * a.N;
         const bool vec = (a.N & 7) == 0;
+        for (int j = 0; j < my_tiles; ++j) {
+            const int buf = j & 1;
+            const int tile = int(blockIdx.x) + j * int(gridDim.x);
+            const int m0 = (tile % a.mt) * TCD_BM, n0 = (tile / a.mt) * BN;
+            if (ok) ok = mbar_wait(&acc_full[buf], (j >> 1) & 1);
+            if (!ok) break;
+            tc_fence_after();
+            const int m = m0 + 32 * warp + lane;
+            T* yrow = reinterpret_cast<T*>(a.y) + size_t(m) * a.N;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(tmem + (uint32_t(32 * warp) << 16) + uint32_t(c0), r);
-            tmem_wait_ld();
-            if (!ok || m >= a.M) continue;
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem + (uint32_t(32 * warp) << 16) + uint32_t(buf * S::ACC_COLS + c0), r);
+                tmem_wait_ld();
+                if (m >= a.M) continue;
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-                const int nn = n0 + c0 + 8 * v;
-                if (c0 + 8 * v >= BN || nn >= a.N) break;
-                uint32_t o[4];
+                for (int v = 0; v < 4; ++v) {
+                    const int nn = n0 + c0 + 8 * v;
+                    if (c0 + 8 * v >= BN || nn >= a.N) break;
+                    uint32_t o[4];
 #pragma unroll
-                for (int q = 0; q < 4; ++q)
-                    o[q] = TR::pack2(__uint_as_float(r[8 * v + 2 * q + 1]), __uint_as_float(r[8 * v + 2 * q]));
-                if (vec && nn + 8 <= a.N) {
-                    *reinterpret_cast<uint4*>(yrow + nn) = make_uint4(o[0], o[1], o[2], o[3]);
-                } else {
-                    for (int q = 0; q < 8; ++q)
-                        if (nn + q < a.N) {
-                            const uint32_t word = o[q >> 1];
-                            reinterpret_cast<uint16_t*>(yrow)[nn + q] =
-                                (q & 1) ? uint16_t(word >> 16) : uint16_t(word & 0xFFFF);
-                        }
+                    for (int q = 0; q < 4; ++q)
+                        o[q] = TR::pack2(__uint_as_float(r[8 * v + 2 * q + 1]), __uint_as_float(r[8 * v + 2 * q]));
+                    if (vec && nn + 8 <= a.N) {
+                        *reinterpret_cast<uint4*>(yrow + nn) = make_uint4(o[0], o[1], o[2], o[3]);
+                    } else {
+                        for (int q = 0; q < 8; ++q)
+                            if (nn + q < a.N) {
+                                const uint32_t word = o[q >> 1];
+                                reinterpret_cast<uint16_t*>(yrow)[nn + q] =
+                                    (q & 1) ? uint16_t(word >> 16) : uint16_t(word & 0xFFFF);
+                            }
+                    }
                 }
             }
+            tc_fence_before();  // (the accumulator reads are complete before the MMA issuer reuses it)
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
     }
     tc_fence_before();
@@ -245,6 +276,8 @@ static int tcd_launch_t(const void* x, const void* wd, void* y, int M, int N, in
     a.N = N;
     a.K = K;
     a.nk = K / TCD_BK;
+    a.mt = (M + TCD_BM - 1) / TCD_BM;
+    a.ntiles = a.mt * ((N + BN - 1) / BN);
     a.y = y;
     CUtensorMap tx, tw;
     {
@@ -261,14 +294,14 @@ static int tcd_launch_t(const void* x, const void* wd, void* y, int M, int N, in
         int rc = make_tmap(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, wd, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
     }
-    const size_t smem = 1024 + size_t(S::NS) * S::STAGE + (2 * S::NS + 2) * 8 + 64;
+    const size_t smem = 1024 + size_t(S::NS) * S::STAGE + (2 * S::NS + 4) * 8 + 64;
     if (smem > device_info().smem_optin) return LQ_E_SHAPE;
     auto kern = tcd_kernel<T, BN>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return LQ_E_CUDA;
     void* args[] = {&tx, &tw, &a};
-    return pdl_launch(reinterpret_cast<const void*>(kern), dim3((M + TCD_BM - 1) / TCD_BM, (N + BN - 1) / BN, 1),
-                      dim3(TCD_THREADS), smem, st, args);
+    const int grid = a.ntiles < device_info().sm_count ? a.ntiles : device_info().sm_count;
+    return pdl_launch(reinterpret_cast<const void*>(kern), dim3(grid, 1, 1), dim3(TCD_THREADS), smem, st, args);
 }
 
 size_t qmm_dense_workspace_bytes(int N, int K) { return size_t(N) * size_t(K) * 2; }
