@@ -210,7 +210,8 @@ def candidates(M: int, K: int, N: int, bits: int = 4, dtype: torch.dtype = torch
     """Tuning candidates for one shape (the analogue of locals/kernels.py:654-674), from the library's own
     list (``lq_list_configs``): decode tilings ("qmv", MT token tiles of 8, WK warps splitting K per
     16-row fragment, KS cluster split-K, NS stages), ("tcv", NTOK token tile, KS split-K, WS weight slots,
-    PERSISTENT) and, from 65 rows, ("tc", BN); 0 = the library's choice."""
+    PERSISTENT), from 65 rows ("tc", BN), and from 128 rows for matrices of at most DENSE_MAX weights ("dense"[, BN])
+    (dequantize once + dense GEMM); 0 = the library's choice."""
     L = _lib.lib()
     n = L.lq_list_configs(M, N, K, bits, 64, dtype_code(dtype), None, 0)
     arr = (_lib.Cfg * max(n, 1))()
@@ -219,6 +220,10 @@ def candidates(M: int, K: int, N: int, bits: int = 4, dtype: torch.dtype = torch
     for c in arr[:n]:
         name = _FAMILY_NAME[c.family]
         out.append((name,) + tuple(int(v) for v in c.p[: _NPARAM[name]]))
+    # the reference's dense prefill path (dequantize + dense GEMM, timed per shape like its own choice between MLX's
+    # quantized GEMM and dequantize + matmul, locals/kernels.py:872-898) from the prefill row count
+    if M >= 128 and N * K <= DENSE_MAX and K % 64 == 0 and N >= 16 and bits in (4, 8):
+        out += [("dense",)] + [("dense", bn) for bn in (224, 256) if N % bn == 0 or bn == 256]
     return out
 
 

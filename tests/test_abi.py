@@ -102,6 +102,9 @@ def test_supported_and_candidates():
     assert all(c[0] != "qmvg" for c in kernels.candidates(32, 2560, 6144, 4))
     pre = kernels.candidates(2048, 4096, 14336, 4)
     assert ("tc", 0) in pre and ("tc", 256) in pre and ("tcv", 256, 1, 0, 0) in pre
+    assert ("dense",) in pre and ("dense", 224) in pre  # the reference's dequantize + dense GEMM path
+    assert all(c[0] != "dense" for c in kernels.candidates(64, 4096, 14336, 4))  # decode sizes: never
+    assert all(c[0] != "dense" for c in kernels.candidates(2048, 16384, 16384, 4))  # past DENSE_MAX weights
     assert L.lq_list_configs(16, 6144, 2560, 4, 64, 1, None, 0) == len(dec)
     assert kernels.candidates(16, 2496, 6144, 4) == [] or all(c[0] != "tcv" for c in kernels.candidates(16, 2496, 6144, 4))
     assert kernels.supported("tc", 2048, 4096, 14336) and not kernels.supported("qmv", 16, 2496, 6144)
