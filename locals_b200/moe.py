@@ -64,6 +64,29 @@ def group(inds: torch.Tensor, E: int):
     return order, starts, experts, nseg, pos
 
 
+# Up to this many tokens a step, each (token, slot) pair is its own segment in pair order and the counting sort is
+# skipped (one launch less): a token's top-k experts are distinct, so every expert's weights are still read once. The
+# reference's own decode path computes each slot straight from its expert the same way (locals/moe.py:243-349).
+DIRECT_MAX_TOKENS = 1
+_DIRECT: dict = {}
+
+
+def direct_grouping(inds: torch.Tensor):
+    """(order, starts, experts, nseg, pos) with one segment a pair, pairs in their own order: order and starts are
+    the identity, experts the pairs' expert ids, pos None (the combine reads row t * k + r)."""
+    flat = inds.reshape(-1).contiguous()
+    _check_cuda(flat)
+    P = flat.numel()
+    key = (P, flat.device)
+    c = _DIRECT.get(key)
+    if c is None:
+        ar = torch.arange(P + 1, dtype=torch.int32, device=flat.device)
+        c = (ar[:P], ar, torch.full((1,), P, dtype=torch.int32, device=flat.device))
+        _DIRECT[key] = c
+    order, starts, nseg = c
+    return order, starts, flat.view(torch.int32), nseg, None
+
+
 def gather(x: torch.Tensor, order: torch.Tensor, k: int) -> torch.Tensor:
     D = x.shape[-1]
     P = order.numel()
@@ -168,6 +191,6 @@ class MoELayer:
         D = x.shape[-1]
         x2 = x.reshape(-1, D).contiguous()
         inds, wts = self.route(x2)
-        grouping = group(inds, self.n_experts)
+        grouping = direct_grouping(inds) if x2.shape[0] <= DIRECT_MAX_TOKENS else group(inds, self.n_experts)
         ys = switch_glu(x2, inds, self.gate, self.up, self.down, self.bits, self.group_size, grouping)
         return combine(ys, wts, grouping[4]).reshape(x.shape)

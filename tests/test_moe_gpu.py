@@ -147,3 +147,25 @@ def test_route_fused(cuda, T):
     i2, w2 = moe.route_topk(moe.router_logits(xt, wt), 4)
     assert np.array_equal(i1.cpu().numpy(), i2.cpu().numpy())
     np.testing.assert_allclose(w1.cpu().numpy(), w2.cpu().numpy(), rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("M", [1, 3])
+def test_direct_grouping_matches_sort(cuda, M):
+    # one segment a (token, slot) pair (no counting sort, the decode path for one token) computes what the sorted
+    # grouping computes; at 3 tokens an expert may appear in two segments and is simply read twice
+    import torch
+    from locals_b200 import moe
+
+    rng = np.random.default_rng(17 + M)
+    E, K, D, I = 64, 4, 2048, 768
+    x, wr = _router_inputs(rng, M, E, D)
+    _, _, _, tg, tu, td = _experts(rng, E, D, I, cuda)
+    xt = x_torch(x, "bfloat16", cuda)
+    inds, wts = moe.route(xt, torch.from_numpy(wr).to(cuda, torch.float16), K)
+    ys_sorted = moe.switch_glu(xt, inds, tg, tu, td, grouping=moe.group(inds, E))
+    y_sorted = moe.combine(ys_sorted, wts, moe.group(inds, E)[4])
+    ys_direct = moe.switch_glu(xt, inds, tg, tu, td, grouping=moe.direct_grouping(inds))
+    y_direct = moe.combine(ys_direct, wts, None)
+    torch.cuda.synchronize()
+    a, b = y_direct.float().cpu().numpy(), y_sorted.float().cpu().numpy()
+    assert rel_err(a, b) <= 1e-3
