@@ -34,28 +34,44 @@ namespace lq {
 
 template <typename T>
 __global__ void __launch_bounds__(256) dequant4_kernel(const uint4* __restrict__ wq, const uint16_t* __restrict__ s,
-                                                       const uint16_t* __restrict__ b, int64_t n_units, int K,
+                                                       const uint16_t* __restrict__ b, uint32_t n_units, uint32_t K,
                                                        uint4* __restrict__ out) {
     using TR = F16Traits<T>;
+    constexpr int UNR = 4;  // units a thread per step: every load is issued before any arithmetic
     grid_dep_wait();
-    const int units_row = K / 32;  // 16-byte units (32 codes) a row
-    for (int64_t u = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; u < n_units; u += int64_t(gridDim.x) * blockDim.x) {
-        const int64_t row = u / units_row;
-        const int piece = int(u - row * units_row);
-        const size_t g = size_t(row) * (K / 64) + (piece >> 1);
-        const uint32_t sv = s[g], bv = b[g];
-        const uint32_t s2 = prmt(sv, sv, 0x1010), b2 = prmt(bv, bv, 0x1010);
-        const uint4 w4 = wq[u];
-        const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
-        uint4* dst = out + u * 4;
+    const uint32_t units_row = K / 32;  // 16-byte units (32 codes) a row
+    const uint32_t groups_row = K / 64;
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t u0 = blockIdx.x * blockDim.x + threadIdx.x; u0 < n_units; u0 += UNR * stride) {
+        uint4 w4[UNR];
+        uint32_t sv[UNR], bv[UNR];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            uint32_t p[4];
+        for (int j = 0; j < UNR; ++j) {
+            const uint32_t u = u0 + j * stride;
+            if (u < n_units) {
+                const uint32_t row = u / units_row, piece = u - row * units_row;
+                const size_t g = size_t(row) * groups_row + (piece >> 1);
+                w4[j] = wq[u];
+                sv[j] = s[g];
+                bv[j] = b[g];
+            }
+        }
 #pragma unroll
-            for (int e = 0; e < 4; ++e)  // codes (e, e + 4) of the word
-                p[e] = TR::sub_magic_fma(lop3_and_or(ws[c] >> (4 * e), 0x000F000Fu, TR::kMagic2), s2, b2);
-            dst[c] = make_uint4(prmt(p[0], p[1], 0x5410), prmt(p[2], p[3], 0x5410), prmt(p[0], p[1], 0x7632),
-                                prmt(p[2], p[3], 0x7632));  // K order (0,1) (2,3) (4,5) (6,7)
+        for (int j = 0; j < UNR; ++j) {
+            const uint32_t u = u0 + j * stride;
+            if (u >= n_units) break;
+            const uint32_t s2 = prmt(sv[j], sv[j], 0x1010), b2 = prmt(bv[j], bv[j], 0x1010);
+            const uint32_t ws[4] = {w4[j].x, w4[j].y, w4[j].z, w4[j].w};
+            uint4* dst = out + size_t(u) * 4;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t p[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e)  // codes (e, e + 4) of the word
+                    p[e] = TR::sub_magic_fma(lop3_and_or(ws[c] >> (4 * e), 0x000F000Fu, TR::kMagic2), s2, b2);
+                dst[c] = make_uint4(prmt(p[0], p[1], 0x5410), prmt(p[2], p[3], 0x5410), prmt(p[0], p[1], 0x7632),
+                                    prmt(p[2], p[3], 0x7632));  // K order (0,1) (2,3) (4,5) (6,7)
+            }
         }
     }
     grid_dep_launch();
@@ -253,15 +269,17 @@ static int pdl_launch(const void* func, dim3 grid, dim3 block, size_t smem, cuda
 
 template <typename T>
 static int dequant4_launch(const uint32_t* w, const void* s, const void* b, int N, int K, void* out, cudaStream_t st) {
-    int64_t n_units = int64_t(N) * (K / 32);
+    const int64_t units = int64_t(N) * (K / 32);
+    if (units >= (int64_t(1) << 31)) return LQ_E_SHAPE;  // (32-bit unit indices)
+    uint32_t n_units = uint32_t(units);
     const int threads = 256;
-    int64_t blocks = (n_units + threads - 1) / threads;
-    const int64_t cap = int64_t(device_info().sm_count) * 8;
+    int64_t blocks = (units + threads - 1) / threads;
+    const int64_t cap = int64_t(device_info().sm_count) * 8;  // 2048 threads a SM, each 4 units a step
     if (blocks > cap) blocks = cap;
     const uint4* wq = reinterpret_cast<const uint4*>(w);
     const uint16_t* sp = static_cast<const uint16_t*>(s);
     const uint16_t* bp = static_cast<const uint16_t*>(b);
-    int K_ = K;
+    uint32_t K_ = uint32_t(K);
     uint4* o = static_cast<uint4*>(out);
     void* args[] = {&wq, &sp, &bp, &n_units, &K_, &o};
     return pdl_launch(reinterpret_cast<const void*>(dequant4_kernel<T>), dim3(unsigned(blocks)), dim3(threads), 0, st,
