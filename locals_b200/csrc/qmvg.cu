@@ -251,9 +251,15 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
                 xb[mt][3][1] = prmt(u1.y, u1.w, 0x7632);
             }
             const uint32_t sb = st + S::W_BYTES + 2 * warp;
+            // All FR fragments run without a branch, so the stage is one straight block whose shared loads the
+            // compiler can issue ahead of the arithmetic. A CTA holding nf = FR - 1 fragments computes one extra
+            // fragment from stale bytes: every address stays inside the stage (weights below (2 FR - 1) * 2048 <
+            // W_BYTES, scales and biases inside their FR * 16-row tables), its partial sums land in rows
+            // [16 nf, 16 FR) of the reduction table and the final sum reads rows below 16 nf only. Those CTAs are
+            // off the critical path (the FR-fragment CTAs set the kernel's length).
 #pragma unroll
             for (int f = 0; f < FR; ++f) {
-                if (f < nf) {
+                {
                     const uint32_t fb = st + f * 2048 + w_off;
                     const uint2 wa = qg_lds64(fb), wb = qg_lds64(fb + 8 * 128);
                     const int ra = 16 * f + g, rb = ra + 8;
