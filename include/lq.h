@@ -186,7 +186,8 @@ size_t lq_kv_attend_workspace(int B, int H, int KVH, int n);
  * The per-block softmax parts go to a 4 MiB buffer inside the library (a __device__ array that every GPU loading
  * the library holds until the process exits); nothing is allocated or freed. Shapes whose parts need more than
  * 4 MiB (lq_kv_attend_workspace(B, H, KVH, n) > 4194304) return LQ_E_SCRATCH before any launch. The first call on a
- * device looks up the buffer's device address (cudaGetSymbolAddress) and should come before any stream capture.
+ * device looks up the buffer's device address (cudaGetSymbolAddress) and should come before any stream capture; the
+ * address is kept for the life of the process, so do not call this again on a device after cudaDeviceReset on it.
  * All calls share the buffer: calls that overlap on the GPU (unordered streams) race and may return wrong
  * results. Other arguments, results and errors as lq_kv_attend. */
 int lq_kv_attend_noalloc(const void* q, const uint32_t* kq, const void* ks, const void* kb, const uint32_t* vq,

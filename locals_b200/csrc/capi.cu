@@ -9,9 +9,6 @@
 #include "qmv.h"
 
 namespace lq {
-void note_cuda_error(cudaError_t e);
-const char* last_cuda_error();
-unsigned int read_status(bool clear);
 int quantize_run(const void* w, int w_dt, int N, int K, int bits, int group, uint32_t* wq, void* s, void* b,
                  int sb_dt, cudaStream_t st);
 int dequantize_run(const uint32_t* wq, const void* s, const void* b, int N, int K, int bits, int group, int dt,
@@ -66,14 +63,6 @@ int scatter_rows_run(const void* src, const int32_t* idx, int R, int row_bytes, 
 
 using namespace lq;
 
-static inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
-
-static inline bool is16(int dt) { return dt == LQ_F16 || dt == LQ_BF16; }
-
-static int finish(int rc) {
-    if (rc == LQ_E_CUDA) note_cuda_error(cudaGetLastError());
-    return rc;
-}
 
 static int check_common(const void* x, const uint32_t* w, const void* s, const void* b, int M, int N, int K, int bits,
                         int group_size, int dtype) {

@@ -443,7 +443,8 @@ size_t kv_attend_workspace_bytes(int B, int H, int KVH, int n, int sms) {
 }
 
 bool kv_attend_shape_ok(int B, int H, int KVH, int n, int cap, int head_dim) {
-    if (B < 1 || H < 1 || KVH < 1 || H % KVH || head_dim != KVA_HD) return false;
+    // B and KVH are the attend kernel's grid z and y (at most 65535 each)
+    if (B < 1 || B > 65535 || H < 1 || KVH < 1 || KVH > 65535 || H % KVH || head_dim != KVA_HD) return false;
     const int G = H / KVH;
     return G <= KVA_MAX_G && n >= 0 && n <= cap && cap >= 1;
 }
@@ -465,13 +466,11 @@ static int kva_launch(K kern, dim3 grid, dim3 block, size_t smem, cudaStream_t s
 
 template <typename T, bool HI>
 static int kva_run_t(const KvaArgs& a, int B, cudaStream_t st) {
-    static bool attr_set = false;  // per instantiation; the attribute is per device function
-    if (!attr_set) {
-        if (cudaFuncSetAttribute(kv_attend_kernel<T, HI>, cudaFuncAttributeMaxDynamicSharedMemorySize, KVA_SMEM) !=
-            cudaSuccess)
-            return LQ_E_CUDA;
-        attr_set = true;
-    }
+    // The shared-memory limit is an attribute of the function on the CURRENT device: set it on every call (a
+    // cheap host call), so a process that attends on several GPUs sets it on each and no host flag is shared.
+    if (cudaFuncSetAttribute(kv_attend_kernel<T, HI>, cudaFuncAttributeMaxDynamicSharedMemorySize, KVA_SMEM) !=
+        cudaSuccess)
+        return LQ_E_CUDA;
     int rc = kva_launch(kv_attend_kernel<T, HI>, dim3(a.nsplit, a.KVH, B), dim3(KVA_NW * 32), KVA_SMEM, st, a);
     if (rc || a.nsplit == 1) return rc;
     return kva_launch(kv_join_kernel<T>, dim3(B * a.H), dim3(KVA_HD), 0, st, a);

@@ -13,14 +13,30 @@
 // In host code `kva_static_scratch` names a host-side shadow, not device memory: handing it to a kernel would fault
 // or, where the GPU can reach host memory, silently use the wrong memory. The device address is therefore looked up
 // with cudaGetSymbolAddress once per device, with that device current, on the first call made on it, and cached.
-// That first call on a device should come before any stream capture.
+// That first call on a device should come before any stream capture. The cache lives as long as the process: a
+// caller that destroys its context on a device (cudaDeviceReset) and then calls this entry point again on that
+// device would be handed the old, stale address, so such callers must not use this entry point after a reset.
 //
 // Every call shares the one array, and nothing in it survives a call in a useful way: each launch writes every part
 // it later reads, so nothing needs clearing first. Calls whose kernels overlap on the GPU (different streams, or
 // different host threads' streams without ordering between them) race on the array and may return wrong results;
 // order them on one stream or use lq_kv_attend with separate workspaces.
 
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <mutex>
+
+#include "../../include/lq.h"
+#include "lq_host.h"
+
 namespace lq {
+bool kv_attend_shape_ok(int B, int H, int KVH, int n, int cap, int head_dim);
+size_t kv_attend_workspace_bytes(int B, int H, int KVH, int n, int sms);
+int kv_attend_run(const void* q, const uint32_t* kq, const void* ks, const void* kb, const uint32_t* vq,
+                  const void* vs, const void* vb, const int32_t* start, int n, const float* sinks, float scale, int B,
+                  int H, int KVH, int cap, int dtype, void* workspace, size_t workspace_bytes, void* out,
+                  cudaStream_t st);
 
 constexpr size_t KVA_STATIC_SCRATCH_BYTES = size_t(4) << 20;
 static __device__ __align__(256) uint8_t kva_static_scratch[KVA_STATIC_SCRATCH_BYTES];
@@ -53,7 +69,9 @@ static int kva_static_scratch_address(void** out) {
 
 }  // namespace lq
 
-int lq_kv_attend_noalloc(const void* q, const uint32_t* kq, const void* ks, const void* kb, const uint32_t* vq,
+using namespace lq;
+
+extern "C" int lq_kv_attend_noalloc(const void* q, const uint32_t* kq, const void* ks, const void* kb, const uint32_t* vq,
                          const void* vs, const void* vb, const int32_t* start, int n, const float* sinks, float scale,
                          int B, int H, int KVH, int cap, int head_dim, int dtype, void* out, void* stream) {
     if (!q || !kq || !ks || !kb || !vq || !vs || !vb || !out) return LQ_E_ARG;

@@ -89,13 +89,35 @@ int check_device() {
     return di.major == 10 ? LQ_OK : LQ_E_DEVICE;
 }
 
+static std::mutex& status_mutex() {
+    static std::mutex m;
+    return m;
+}
+
+static StatusReader* status_readers(int** count) {
+    static StatusReader readers[64];
+    static int n = 0;
+    *count = &n;
+    return readers;
+}
+
+void register_status_reader(StatusReader r) {
+    std::lock_guard<std::mutex> lock(status_mutex());
+    int* n = nullptr;
+    StatusReader* readers = status_readers(&n);
+    if (*n < 64) readers[(*n)++] = r;
+}
+
 unsigned int read_status(bool clear) {
     if (cudaDeviceSynchronize() != cudaSuccess) return 0xffffffffu;
+    std::lock_guard<std::mutex> lock(status_mutex());
+    int* n = nullptr;
+    StatusReader* readers = status_readers(&n);
     unsigned int v = 0;
-    if (cudaMemcpyFromSymbol(&v, g_status, sizeof(v)) != cudaSuccess) return 0xffffffffu;
-    if (clear) {
-        const unsigned int z = 0;
-        if (cudaMemcpyToSymbol(g_status, &z, sizeof(z)) != cudaSuccess) return 0xffffffffu;
+    for (int i = 0; i < *n; ++i) {
+        const unsigned int w = readers[i](clear);
+        if (w == 0xffffffffu) return w;
+        v |= w;
     }
     return v;
 }

@@ -32,4 +32,17 @@ int check_device();
 
 inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? LQ_OK : LQ_E_CUDA; }
 
+// The last CUDA error the library saw (for lq_last_cuda_error) and the device status words.
+void note_cuda_error(cudaError_t e);
+const char* last_cuda_error();
+unsigned int read_status(bool clear);
+
+// Argument-check helpers of the C ABI's entry points.
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+inline bool is16(int dt) { return dt == LQ_F16 || dt == LQ_BF16; }
+inline int finish(int rc) {
+    if (rc == LQ_E_CUDA) note_cuda_error(cudaGetLastError());
+    return rc;
+}
+
 }  // namespace lq

@@ -24,6 +24,7 @@
 #include "lq_ptx.cuh"
 #include "lq_status.cuh"
 #include "qmv.h"
+#include "tcv_common.cuh"
 
 namespace lq {
 

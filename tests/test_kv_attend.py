@@ -96,3 +96,19 @@ def test_kv_attend_abi_rejects_bad_arguments():
     assert rc(H=30, KVH=4) == _lib.LQ_E_SHAPE
     assert rc(n=257) == _lib.LQ_E_SHAPE
     assert rc(n=-1) == _lib.LQ_E_SHAPE
+    assert rc(B=65536) == _lib.LQ_E_SHAPE  # B is the attend kernel's grid z (at most 65535)
+    assert rc(H=65536 * 2, KVH=65536) == _lib.LQ_E_SHAPE  # KVH is its grid y
+
+
+def test_kv_attend_noalloc_abi_rejects_bad_arguments():
+    L = _lib.lib()
+    fake = ctypes.c_void_p(4096)
+
+    def rc(B=1, H=32, KVH=4, n=10, cap=256, hd=128, dtype=_lib.BF16, q=fake):
+        return L.lq_kv_attend_noalloc(q, fake, fake, fake, fake, fake, fake, None, n, None, 0.1, B, H, KVH, cap, hd,
+                                      dtype, fake, None)
+
+    assert rc(q=None) == _lib.LQ_E_ARG
+    assert rc(dtype=_lib.F32) == _lib.LQ_E_UNSUPPORTED
+    assert rc(B=65536) == _lib.LQ_E_SHAPE
+    assert rc(n=257) == _lib.LQ_E_SHAPE

@@ -70,6 +70,42 @@ def test_noalloc_matches_workspace_entry_point(cuda, first, second):
         assert err <= TOL_REL * m, (i, err, m)
 
 
+def test_noalloc_on_a_second_device():
+    """With two or more GPUs visible, the same check on device 1 after device 0 in one process: the buffer's address
+    and the kernel's shared-memory attribute are per device, so device 1 must get its own (plain per-device calls, no
+    peer memory)."""
+    import torch
+    from locals_b200 import _lib
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("one GPU visible")
+    L = _lib.lib()
+    B, H, KVH, n, cap, pads = 2, 32, 4, 5000, 5120, [0, 333]
+    prev = torch.cuda.current_device()
+    try:
+        for d in (0, 1):
+            dev = torch.device("cuda", d)
+            torch.cuda.set_device(dev)
+            q, keys, values, sinks = _cache(dev, B, H, KVH, cap, 200 + d)
+            start = torch.tensor(pads, dtype=torch.int32, device=dev)
+            args = _args(q, keys, values, start, n, sinks, B, H, KVH, cap)
+            need = L.lq_kv_attend_workspace(B, H, KVH, n)
+            ws = torch.empty(need, dtype=torch.uint8, device=dev)
+            ref = torch.empty((B, H, 1, 128), dtype=torch.bfloat16, device=dev)
+            got = torch.full((B, H, 1, 128), float("nan"), dtype=torch.bfloat16, device=dev)
+            stream = torch.cuda.current_stream(dev).cuda_stream
+            assert L.lq_kv_attend(*args, ws.data_ptr(), need, ref.data_ptr(), stream) == _lib.LQ_OK
+            assert L.lq_kv_attend_noalloc(*args, got.data_ptr(), stream) == _lib.LQ_OK
+            torch.cuda.synchronize(dev)
+            assert _lib.device_status() == 0
+            ref32, got32 = ref.float(), got.float()
+            assert torch.isfinite(got32).all()
+            err, m = (got32 - ref32).abs().max().item(), ref32.abs().max().item()
+            assert err <= TOL_REL * m, (d, err, m)
+    finally:
+        torch.cuda.set_device(prev)
+
+
 def test_noalloc_refuses_shapes_beyond_its_buffer(cuda):
     import torch
     from locals_b200 import _lib
