@@ -146,7 +146,11 @@ static int qmm_common(const void* x, const uint32_t* w, const void* s, const voi
         rc = qmvg_run(x, w, s, b, nout, outs, a.seg_end, a.ldo, M, N, K, dtype, p, st);
         if (rc != LQ_E_SHAPE) return finish(rc);
     }
-    if (!qmv_shape_ok(K, bits)) return LQ_E_SHAPE;
+    if (!qmv_shape_ok(K, bits)) {
+        // a 4-bit K that is a multiple of 128 but not of 256: the tensor-core family
+        if (fam != LQ_FAM_AUTO || !tcv_shape_ok(M, K, bits)) return LQ_E_SHAPE;
+        return finish(tcv_run(x, M, mats, 1, N, K, nout, outs, a.seg_end, a.ldo, bits, dtype, nullptr, st));
+    }
     return finish(qmv_run(x, M, mats, 1, a, bits, dtype, (cfg && fam == LQ_FAM_QMV) ? cfg->p : nullptr, M, 1, st));
 }
 
@@ -317,7 +321,7 @@ int lq_moe_experts(const void* xs, const int32_t* starts, const int32_t* experts
     if (glu && (!w1 || !s1 || !b1)) return LQ_E_ARG;
     if (glu && (!aligned(w1, 16) || !aligned(s1, 4) || !aligned(b1, 4))) return LQ_E_ALIGN;
     if (E < 1 || max_rows < 1) return LQ_E_SHAPE;
-    if (!qmv_shape_ok(K, bits)) return LQ_E_SHAPE;
+    if (!qmv_shape_ok(K, bits) && (gather_order || !tcv_shape_ok(P, K, bits))) return LQ_E_SHAPE;
     if (int64_t(E) * N > INT32_MAX) return LQ_E_SHAPE;
     QmvArgs a = {};
     a.M = P;
@@ -344,7 +348,9 @@ int lq_moe_experts(const void* xs, const int32_t* starts, const int32_t* experts
     // from 1024 routed rows (about 16 per expert at 64 experts) the expert GEMMs run on the tensor-core
     // family, persistent when K allows (pre-gathered rows only); below that the mma.sync family's grouped
     // mode measured faster on B200
-    if (!gather_order && P >= 1024) {
+    // K the mma.sync family does not take (a 4-bit K that is a multiple of 128 but not of 256, e.g. an expert
+    // intermediate of 384): the tensor-core family at any row count
+    if (!gather_order && (P >= 1024 || !qmv_shape_ok(K, bits))) {
         const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
         if (tcvp_shape_ok(P, K, bits)) {  // persistent: one CTA per SM walks the expert tiles
             rc = tcvp_run_grouped(xs, P, m, glu ? 2 : 1, N, K, out, starts, experts, nseg, E, bits, dtype, 0, st);

@@ -158,8 +158,22 @@ def route(x: torch.Tensor, w: torch.Tensor, k: int, mode: int = SOFTMAX):
 
 def switch_glu(x: torch.Tensor, inds: torch.Tensor, gate, up, down, bits: int = 4, group_size: int = 64,
                grouping=None) -> torch.Tensor:
-    """mlx-lm SwitchGLU for rows x (M, D) and experts inds (M, k): (M*k, D) rows in pair order, with the
-    grouping used (the reference's switch_glu, locals/moe_kernel.py:230-239)."""
+    """mlx-lm SwitchGLU for rows x (M, D) and experts inds (M, k): (M, k, D), slot r of token t in row (t, r) (the
+    reference's switch_glu, locals/moe_kernel.py:230-239, which returns the pairs in their own order)."""
+    M, k = inds.shape
+    if grouping is None:
+        grouping = group(inds, gate[0].shape[0])
+    ys = switch_glu_grouped(x, inds, gate, up, down, bits, group_size, grouping)
+    pos = grouping[4]
+    if pos is not None:  # expert order -> pair order: row j of the result is row pos[j] of ys
+        ys = gather(ys, pos, 1)
+    return ys.reshape(M, k, -1)
+
+
+def switch_glu_grouped(x: torch.Tensor, inds: torch.Tensor, gate, up, down, bits: int = 4, group_size: int = 64,
+                       grouping=None) -> torch.Tensor:
+    """SwitchGLU with its (M*k, D) rows left in the grouping's expert order (row order[j] of the pairs in row j; the
+    combine reads them back through the inverse permutation pos)."""
     M, k = inds.shape
     E = gate[0].shape[0]
     I = gate[0].shape[1]
@@ -192,5 +206,5 @@ class MoELayer:
         x2 = x.reshape(-1, D).contiguous()
         inds, wts = self.route(x2)
         grouping = direct_grouping(inds) if x2.shape[0] <= DIRECT_MAX_TOKENS else group(inds, self.n_experts)
-        ys = switch_glu(x2, inds, self.gate, self.up, self.down, self.bits, self.group_size, grouping)
+        ys = switch_glu_grouped(x2, inds, self.gate, self.up, self.down, self.bits, self.group_size, grouping)
         return combine(ys, wts, grouping[4]).reshape(x.shape)

@@ -162,10 +162,14 @@ def test_direct_grouping_matches_sort(cuda, M):
     _, _, _, tg, tu, td = _experts(rng, E, D, I, cuda)
     xt = x_torch(x, "bfloat16", cuda)
     inds, wts = moe.route(xt, torch.from_numpy(wr).to(cuda, torch.float16), K)
-    ys_sorted = moe.switch_glu(xt, inds, tg, tu, td, grouping=moe.group(inds, E))
-    y_sorted = moe.combine(ys_sorted, wts, moe.group(inds, E)[4])
+    grouping = moe.group(inds, E)
+    ys_sorted = moe.switch_glu_grouped(xt, inds, tg, tu, td, grouping=grouping)  # expert order
+    y_sorted = moe.combine(ys_sorted, wts, grouping[4])
+    ys_pairs = moe.switch_glu(xt, inds, tg, tu, td, grouping=grouping)  # pair order (M, k, D)
+    y_pairs = moe.combine(ys_pairs.reshape(M * K, D), wts, None)
     ys_direct = moe.switch_glu(xt, inds, tg, tu, td, grouping=moe.direct_grouping(inds))
-    y_direct = moe.combine(ys_direct, wts, None)
+    y_direct = moe.combine(ys_direct.reshape(M * K, D), wts, None)
+    assert torch.equal(y_pairs, y_sorted)  # the same rows, only reordered
     torch.cuda.synchronize()
     a, b = y_direct.float().cpu().numpy(), y_sorted.float().cpu().numpy()
     assert rel_err(a, b) <= 1e-3
