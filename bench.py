@@ -587,6 +587,7 @@ CASES = {
     "qkv16_l2": "fused QKV decode at M=16 (the library's choice, qmvg) over 24 layers (218 MB > L2), for DRAM figures",
     "qkv1_l2": "fused QKV decode at M=1 (the group-per-warp qmvg kernel) over 24 layers (218 MB > L2)",
     "mlp64": "8-bit MLP gate||up + SiLU.mul and down at M=64, 4 layers",
+    "mlp1": "8-bit MLP gate||up + SiLU.mul and down at M=1, 4 layers (320 MB > L2)",
     "tc": "prefill GEMM x bf16 [1024,4096] . 4-bit [7168,4096]^T",
     "moe16": "MoE layer, 64 experts top-4, D 2048, I 768, M=16",
     "moe512": "MoE layer, 64 experts top-4, D 2048, I 768, M=512",
@@ -612,10 +613,10 @@ def run_case(name):
         for _ in range(3):
             for w, s, b in Ws:
                 kernels.qmm_split(x, w, s, b, HEAD_WIDTHS)
-    elif name == "mlp64":
+    elif name in ("mlp64", "mlp1"):
         mlps = [FusedMLP(*[QuantizedLinear(*make_layer(torch, n, k, 8, torch.bfloat16, gen, dev), bits=8)
                            for n, k in ((9728, 2560), (9728, 2560), (2560, 9728))]) for _ in range(4)]
-        x = torch.randn((64, 2560), generator=gen, device=dev).to(torch.bfloat16)
+        x = torch.randn((64 if name == "mlp64" else 1, 2560), generator=gen, device=dev).to(torch.bfloat16)
         for _ in range(2):
             for m in mlps:
                 m(x)

@@ -141,6 +141,18 @@ int lq_moe_experts(const void* xs, const int32_t* starts, const int32_t* experts
                    const void* s1, const void* b1, void* out, int E, int N, int K, int bits, int group_size, int dtype,
                    const int32_t* gather_order, int gather_k, void* stream);
 
+/* The down projection and the weighted combine of ONE token's k slots in one launch (decode; 4-bit, k <= 4):
+ * y (1, N) = sum over slots r of weights[r] * round(h[pos[r]] . down_e^T), e = experts[pos[r]], the products rounded
+ * to dtype and summed in float32 in slot order, then rounded -- lq_moe_experts (glu = 0) followed by lq_moe_combine
+ * without the (k, N) round trip. Replaces the reference's experts_down and its combine kernel for one token
+ * (locals/moe.py:465-512, 339-348). h (k, K) holds the token's k pairs in the grouping's order, one pair a segment (the order of
+ * lq_moe_group, or the pairs' own order with experts = the token's k expert ids and pos = NULL); w, s, b are the
+ * stacked (E, N, ...) down experts. K % 256 == 0, N % 16 == 0. LQ_E_SHAPE for shapes outside this (use the two
+ * calls then). */
+int lq_moe_down_combine(const void* h, const int32_t* experts, const int32_t* pos, const float* weights,
+                        const uint32_t* w, const void* s, const void* b, void* y, int k, int E, int N, int K, int bits,
+                        int group_size, int dtype, void* stream);
+
 /* y (T, D) = sum over slots r of weights[t, r] * ys[pos[t*k + r], :] in float32, slots in order, rounded
  * to dtype (locals/moe.py:339-348). pos == NULL reads row t*k + r. */
 int lq_moe_combine(const void* ys, const float* weights, const int32_t* pos, void* y, int T, int k, int D, int dtype,

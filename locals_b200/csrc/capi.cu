@@ -47,6 +47,10 @@ int qmm_dense_run(const void* x, const uint32_t* w, const void* s, const void* b
 bool qmvg_shape_ok(int M, int K, int bits);
 int qmvg_run(const void* x, const uint32_t* w, const void* s, const void* b, int nout, void* const* outs,
              const int* seg_end, const int* ldo, int M, int N, int K, int dtype, const int* p, cudaStream_t st);
+bool qmvg_moe_ok(int mode, int k, int rows_e, int K, int sms);
+int qmvg_moe_run(int mode, const void* x, const int32_t* experts, const int32_t* pos, const float* wts,
+                 const uint32_t* w0, const void* s0, const void* b0, const uint32_t* w1, const void* s1, const void* b1,
+                 void* out, int k, int E, int rows_e, int K, int dtype, cudaStream_t st);
 bool kv_attend_shape_ok(int B, int H, int KVH, int n, int cap, int head_dim);
 size_t kv_attend_workspace_bytes(int B, int H, int KVH, int n, int sms);
 int kv_attend_run(const void* q, const uint32_t* kq, const void* ks, const void* kb, const uint32_t* vq,
@@ -345,6 +349,14 @@ int lq_moe_experts(const void* xs, const int32_t* starts, const int32_t* experts
     m.b[1] = glu ? b1 : b0;
     m.rows_total[0] = m.rows_total[1] = E * N;
     if (gather_order && gather_k < 1) return LQ_E_ARG;
+    // one token (P == k pairs, its experts distinct, so every segment holds one pair): the gate/up projections of
+    // the k experts run as one fragment-spread 4-bit decode launch over all SMs (qmvg's MoE mode)
+    if (glu && gather_order && P == gather_k && bits == 4 &&
+        qmvg_moe_ok(1, gather_k, N, K, device_info().sm_count)) {
+        rc = qmvg_moe_run(1, xs, experts, nullptr, nullptr, w0, s0, b0, w1, s1, b1, out, gather_k, E, N, K, dtype,
+                          reinterpret_cast<cudaStream_t>(stream));
+        if (rc != LQ_E_SHAPE) return finish(rc);
+    }
     // from 1024 routed rows (about 16 per expert at 64 experts) the expert GEMMs run on the tensor-core
     // family, persistent when K allows (pre-gathered rows only); below that the mma.sync family's grouped
     // mode measured faster on B200
@@ -366,6 +378,19 @@ int lq_moe_experts(const void* xs, const int32_t* starts, const int32_t* experts
     const int nseg_grid = (E + 1) < P ? (E + 1) : P;  // (one more for a padding bucket, expert id E)
     return finish(qmv_run(xs, gather_order ? 1 : P, m, glu ? 2 : 1, a, bits, dtype, nullptr, max_rows, nseg_grid,
                           reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int lq_moe_down_combine(const void* h, const int32_t* experts, const int32_t* pos, const float* weights,
+                        const uint32_t* w, const void* s, const void* b, void* y, int k, int E, int N, int K, int bits,
+                        int group_size, int dtype, void* stream) {
+    int rc = check_common(h, w, s, b, k, N, K, bits, group_size, dtype);
+    if (rc) return rc;
+    if (!experts || !weights || !y) return LQ_E_ARG;
+    if (E < 1 || int64_t(E) * N > INT32_MAX) return LQ_E_SHAPE;
+    if (bits != 4 || !qmvg_moe_ok(2, k, N, K, device_info().sm_count)) return LQ_E_SHAPE;
+    if (!aligned(y, 2) || !aligned(weights, 4) || !aligned(experts, 4) || !aligned(pos, 4)) return LQ_E_ALIGN;
+    return finish(qmvg_moe_run(2, h, experts, pos, weights, w, s, b, nullptr, nullptr, nullptr, y, k, E, N, K, dtype,
+                               reinterpret_cast<cudaStream_t>(stream)));
 }
 
 int lq_add_rms_norm(const void* x, const void* r, const void* w, void* h, void* n, int rows, int D, float eps,

@@ -284,46 +284,29 @@ __global__ void combine_kernel(const uint16_t* ys, const float* w, const int32_t
     }
 }
 
-// Router logits and top-k of one token per CTA (256 threads): warps compute the E float32 dot products
-// (16-byte loads of x and of each expert's router row; 16 warps, each expert's row split over a warp),
-// the logits stay in shared memory, and warp 0 picks the top k exactly as route_topk_kernel does.
-// logits_out may be null.
+// Router logits and top-k, the experts split over a cluster of RC_CL CTAs and the tokens in tiles of RC_TT (grid
+// (ceil(T / RC_TT), RC_CL), cluster (1, RC_CL, 1), 256 threads). Each CTA stages its E / RC_CL experts' router rows in
+// shared memory BEFORE waiting for the previous kernel (they do not depend on it; at config 4 a CTA's 8 rows are
+// 32 KB, so the weights are read by eight SMs at once instead of one), computes the float32 dot products of its
+// experts with the tile's tokens (16-byte loads, one warp a (token, expert)), and keeps the logits in shared memory.
+// After a cluster barrier warp t of CTA 0 reads token t's E logits from the eight CTAs (distributed shared memory)
+// and picks the top k exactly as route_topk_kernel does. logits_out may be null.
 constexpr int ROUTE_MAX_E = 1024;
-__global__ void __launch_bounds__(512) router_topk_kernel(const void* x, int x_dt, const void* w, int w_dt, int T,
-                                                          int E, int D, int k, int mode, uint32_t* inds, float* weights,
-                                                          float* logits_out) {
-    grid_dep_wait();
-    grid_dep_launch();
-    __shared__ float lg[ROUTE_MAX_E];
-    const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (t >= T) return;
-    const uint4* xr = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + size_t(t) * D);
-    for (int e = warp; e < E; e += 16) {
-        const uint4* wr = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(w) + size_t(e) * D);
-        float acc = 0.0f;
-        for (int i = lane; i < D / 8; i += 32) {
-            float xf[8], wf[8];
-            unpack8(xr[i], x_dt, xf);
-            unpack8(wr[i], w_dt, wf);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) acc = fmaf(xf[j], wf[j], acc);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (lane == 0) {
-            lg[e] = acc;
-            if (logits_out) logits_out[size_t(t) * E + e] = acc;
-        }
-    }
-    __syncthreads();
-    if (warp != 0) return;
+constexpr int RC_CL = 8;
+constexpr int RC_TT = 8;
+constexpr size_t RC_STAGE_MAX = 64 * 1024;
+
+// softmax (mode 0) or sigmoid (mode 1, NaN -> 0) of the E logits fetched by get(e), then the top k
+template <typename Get>
+__device__ __forceinline__ void score_and_select(Get get, int E, int k, int mode, int lane, uint32_t* inds,
+                                                 float* weights) {
     const int per = (E + 31) / 32;
     float sc[TOPK_MAX_PER_LANE];
     if (mode == 0) {
         float mx = -INFINITY;
         for (int j = 0; j < per; ++j) {
             const int e = lane + 32 * j;
-            sc[j] = e < E ? lg[e] : -INFINITY;
+            sc[j] = e < E ? get(e) : -INFINITY;
             mx = fmaxf(mx, sc[j]);
         }
 #pragma unroll
@@ -343,17 +326,111 @@ __global__ void __launch_bounds__(512) router_topk_kernel(const void* x, int x_d
     } else {
         for (int j = 0; j < per; ++j) {
             const int e = lane + 32 * j;
-            const float v = e < E ? 1.0f / (1.0f + expf(-lg[e])) : -1.0f;
+            const float v = e < E ? 1.0f / (1.0f + expf(-get(e))) : -1.0f;
             sc[j] = e < E ? (isnan(v) ? 0.0f : v) : -1.0f;
         }
     }
-    topk_select(sc, per, E, k, lane, inds + size_t(t) * k, weights + size_t(t) * k);
+    topk_select(sc, per, E, k, lane, inds, weights);
+}
+
+__global__ void __launch_bounds__(256) router_topk_kernel(const void* x, int x_dt, const void* w, int w_dt, int T,
+                                                          int E, int D, int k, int mode, int staged, uint32_t* inds,
+                                                          float* weights, float* logits_out) {
+    extern __shared__ __align__(16) uint8_t rsm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rank = int(cluster_ctarank());
+    const int EC = (E + RC_CL - 1) / RC_CL;
+    const int e0 = rank * EC;
+    const int ne = E - e0 < EC ? (E - e0 > 0 ? E - e0 : 0) : EC;
+    float* lg = reinterpret_cast<float*>(rsm);  // [RC_TT][EC]
+    const size_t lg_bytes = (size_t(RC_TT) * EC * 4 + 15) / 16 * 16;
+    const uint16_t* wrows = reinterpret_cast<const uint16_t*>(w) + size_t(e0) * D;
+    uint16_t* wsm = reinterpret_cast<uint16_t*>(rsm + lg_bytes);
+    const size_t wbytes = (staged & 1) ? (size_t(EC) * D * 2 + 15) / 16 * 16 : 0;
+    uint16_t* xsm = reinterpret_cast<uint16_t*>(rsm + lg_bytes + wbytes);  // the tile's tokens (staged & 2)
+    if (staged & 1) {  // this CTA's router rows (independent of the previous kernel)
+        const int n16 = ne * D / 8;
+        for (int i = threadIdx.x; i < n16; i += blockDim.x) cp_async(smem_u32(wsm + 8 * i), wrows + 8 * i, 16, true);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    grid_dep_wait();
+    grid_dep_launch();
+    const int t0 = blockIdx.x * RC_TT;
+    const int tt = T - t0 < RC_TT ? T - t0 : RC_TT;
+    const uint16_t* xtile = reinterpret_cast<const uint16_t*>(x) + size_t(t0) * D;
+    if (staged & 2) {  // the tile's tokens, every 16-byte load in flight at once
+        const int n16 = tt * D / 8;
+        for (int i = threadIdx.x; i < n16; i += blockDim.x) cp_async(smem_u32(xsm + 8 * i), xtile + 8 * i, 16, true);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    if (staged) asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    const uint16_t* wsrc = (staged & 1) ? wsm : wrows;
+    const uint16_t* xsrc = (staged & 2) ? xsm : xtile;
+    for (int it = warp; it < tt * ne; it += 8) {
+        const int tl = it / ne, el = it - tl * ne;
+        const uint4* xr = reinterpret_cast<const uint4*>(xsrc + size_t(tl) * D);
+        const uint4* wr = reinterpret_cast<const uint4*>(wsrc + size_t(el) * D);
+        float acc = 0.0f;
+#pragma unroll 4
+        for (int i = lane; i < D / 8; i += 32) {
+            float xf[8], wf[8];
+            unpack8(xr[i], x_dt, xf);
+            unpack8(wr[i], w_dt, wf);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc = fmaf(xf[j], wf[j], acc);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) {
+            lg[tl * EC + el] = acc;
+            if (logits_out) logits_out[size_t(t0 + tl) * E + e0 + el] = acc;
+        }
+    }
+    cluster_sync();  // every CTA's logits are visible to the cluster
+    if (rank == 0 && warp < tt) {
+        const uint32_t base = smem_u32(lg + warp * EC);
+        auto get = [&](int e) {
+            const int owner = e / EC;
+            return ld_dsmem_f(map_peer(base + 4u * uint32_t(e - owner * EC), uint32_t(owner)));
+        };
+        const int t = t0 + warp;
+        score_and_select(get, E, k, mode, lane, inds + size_t(t) * k, weights + size_t(t) * k);
+    }
+    cluster_sync();  // peers keep their shared memory until CTA 0 has read it
 }
 
 int router_topk_run(const void* x, int x_dt, const void* w, int w_dt, int T, int E, int D, int k, int mode,
                     uint32_t* inds, float* weights, float* logits, cudaStream_t st) {
-    return launch_pdl(router_topk_kernel, dim3(T), dim3(512), 0, st, x, x_dt, w, w_dt, T, E, D, k, mode, inds, weights,
-                      logits);
+    const int EC = (E + RC_CL - 1) / RC_CL;
+    const size_t lg_bytes = (size_t(RC_TT) * EC * 4 + 15) / 16 * 16;
+    const size_t wbytes = (size_t(EC) * D * 2 + 15) / 16 * 16;
+    const size_t xbytes = size_t(RC_TT) * D * 2;
+    // bit 0: router rows staged in shared memory; bit 1: the tile's tokens too (x is 16-byte aligned, D % 8 == 0)
+    const int staged = ((wbytes <= RC_STAGE_MAX && (reinterpret_cast<uintptr_t>(w) % 16) == 0) ? 1 : 0) |
+                       (xbytes <= RC_STAGE_MAX ? 2 : 0);
+    const size_t smem = lg_bytes + ((staged & 1) ? wbytes : 0) + ((staged & 2) ? xbytes : 0);
+    if (smem > 48 * 1024) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(router_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return LQ_E_CUDA;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((T + RC_TT - 1) / RC_TT, RC_CL, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = RC_CL;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cuda_status(cudaLaunchKernelEx(&cfg, router_topk_kernel, x, x_dt, w, w_dt, T, E, D, k, mode, staged, inds,
+                                          weights, logits));
 }
 
 int router_logits_run(const void* x, int x_dt, const void* w, int w_dt, float* logits, int T, int E, int D,

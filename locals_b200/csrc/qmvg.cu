@@ -56,8 +56,25 @@ struct QgShape {
     static_assert(W_FRAG % 1024 == 0, "1 KB alignment of swizzled tiles");
 };
 
+// MoE decode modes (one token, its k routed (token, slot) pairs; the segments of the expert grouping hold one pair
+// each): MOE_GLU -- unit u = (segment u / fpe, fragment u % fpe) of the gate and up stacks of expert experts[seg],
+// output h[seg] = swiglu(gate, up); MOE_COMBINE -- unit u = output fragment u of all k slots' down matrices (fragment
+// r of a unit uses expert experts[r] and x row r = h[r], which sits in MMA token column r), output
+// y = sum_r w[r] * round(y_r) in slot order (the combine of locals/moe.py:339-348 in the down kernel's epilogue).
+constexpr int QG_DENSE = 0, QG_MOE_GLU = 1, QG_MOE_COMBINE = 2;
+
 struct QgArgs {
     int M, N, K;
+    int mode;             // QG_DENSE / QG_MOE_GLU / QG_MOE_COMBINE
+    int fpu;              // fragments per unit (1 dense, 2 GLU, k combine)
+    int units;            // units of the launch
+    int fpe;              // MoE: fragments per expert matrix (rows per expert / 16)
+    int rows_e;           // MoE: rows per expert matrix
+    const int32_t* experts;  // MoE: expert of each segment (one pair a segment, in the grouping's order)
+    const int32_t* pos;   // MOE_COMBINE: slot r's row of h (null: row r)
+    const float* wts;     // MOE_COMBINE: the token's k slot weights
+    const void* s1;       // MOE_GLU: the up stack's scales and biases
+    const void* b1;
     int kg;      // groups a row (K / 64)
     int nchunk;  // stages of 512 K values
     int nfrag;   // 16-row fragments (ceil(N / 16))
@@ -112,6 +129,22 @@ __device__ __forceinline__ void qg_store(const QgArgs& a, int row, int n, float 
         reinterpret_cast<__half*>(base)[off] = __float2half_rn(v);
 }
 
+template <typename T>
+__device__ __forceinline__ float qg_round(float v) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value)
+        return __bfloat162float(__float2bfloat16_rn(v));
+    else
+        return __half2float(__float2half_rn(v));
+}
+
+// silu(g) * u with the activation-dtype rounding points of locals/moe.py:284-289 (the store rounds the product)
+template <typename T>
+__device__ __forceinline__ float qg_swiglu(float g, float u) {
+    const float gt = qg_round<T>(g), ut = qg_round<T>(u);
+    const float sig = qg_round<T>(1.0f / (1.0f + expf(-gt)));
+    return qg_round<T>(gt * sig) * ut;
+}
+
 template <typename T, int MT, int FR>
 __global__ void __launch_bounds__(QG_THREADS, 2)
     qmvg_kernel(const __grid_constant__ CUtensorMap tm_w_full, const __grid_constant__ CUtensorMap tm_w_less,
@@ -129,9 +162,13 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
     uint64_t* empty = full + QG_MAX_STAGES;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int f0 = int((long long)blockIdx.x * a.nfrag / gridDim.x);
-    const int nf = int((long long)(blockIdx.x + 1) * a.nfrag / gridDim.x) - f0;  // FR or FR - 1 (host-chosen grid)
-    if (nf < 1 || nf > FR || nf < FR - 1) {  // the weight box has 16 FR or 16 (FR - 1) rows: nothing else fits
+    const bool moe = a.mode != QG_DENSE;
+    // units [u0, u0 + nu) of fpu fragments each: a CTA holds FR or FR - fpu fragments (host-chosen grid)
+    const int u0 = int((long long)blockIdx.x * a.units / gridDim.x);
+    const int nu = int((long long)(blockIdx.x + 1) * a.units / gridDim.x) - u0;
+    const int f0 = u0 * a.fpu;
+    const int nf = nu * a.fpu;
+    if (nf < 1 || nf > FR || nf < FR - a.fpu) {  // the weight boxes hold 16 FR or 16 (FR - fpu) rows: nothing else fits
         if (threadIdx.x == 0) record_status(LQ_DEV_BOUNDS);
         return;
     }
@@ -152,8 +189,44 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
     if (warp == QG_CW) {
         // ------------------------------ producer warp ------------------------------
         const uint64_t pol_w = policy_evict_first();
-        const CUtensorMap* tm_w = nf == FR ? &tm_w_full : &tm_w_less;  // box of 16 FR or 16 (FR - 1) rows
-        if (lane == 0) prefetch_tmap(tm_w);
+        // dense: one box of 16 FR or 16 (FR - 1) rows; MoE: one 16-row box a fragment from matrix 0 or 1
+        const CUtensorMap* tm_w = nf == FR ? &tm_w_full : &tm_w_less;
+        if (lane == 0) {
+            prefetch_tmap(&tm_w_full);
+            prefetch_tmap(&tm_w_less);
+        }
+        // MoE: each fragment's first row in its stack and its matrix (0: gate or down, 1: up); the experts come from the
+        // routing kernel, so these loads wait for it
+        int frow[FR], fmat[FR];
+#pragma unroll
+        for (int i = 0; i < FR; ++i) {
+            frow[i] = row0 + 16 * i;
+            fmat[i] = 0;
+        }
+        if (moe) {
+            grid_dep_wait();
+#pragma unroll
+            for (int i = 0; i < FR; ++i) {
+                const int j = f0 + (i < nf ? i : nf - 1);  // (the unused slots repeat the last fragment)
+                int seg, fe;
+                if (a.mode == QG_MOE_GLU) {
+                    const int u = j >> 1;
+                    seg = u / a.fpe;
+                    fe = u - seg * a.fpe;
+                    fmat[i] = j & 1;
+                } else {
+                    const int u = j / a.fpu, r = j - u * a.fpu;
+                    seg = a.pos ? a.pos[r] : r;
+                    fe = u;
+                }
+                int e = a.experts[seg];
+                if (e < 0 || (e + 1) * a.rows_e > a.N) {
+                    if (lane == 0) record_status(LQ_DEV_BOUNDS);
+                    e = 0;
+                }
+                frow[i] = e * a.rows_e + 16 * fe;
+            }
+        }
         const uint32_t smem_base = smem_u32(smem);
         const int vb = a.sb_vec;
         const int units = 16 / vb;
@@ -161,13 +234,29 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
             uint8_t* st = smem + s * S::STAGE_BYTES;
             if (lane == 0) {
                 mbar_arrive_expect_tx(&full[s], nf * S::W_FRAG);
-                tma_load_3d(st, tm_w, &full[s], 0, row0, 2 * c, pol_w);
+                if (!moe) {
+                    tma_load_3d(st, tm_w, &full[s], 0, row0, 2 * c, pol_w);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < FR; ++i)
+                        if (i < nf)
+                            tma_load_3d(st + i * S::W_FRAG, fmat[i] ? &tm_w_less : &tm_w_full, &full[s], 0, frow[i], 2 * c,
+                                        pol_w);
+                }
             }
             const uint32_t sdst = smem_base + s * S::STAGE_BYTES + S::W_BYTES;
-            const uint8_t* sbase = reinterpret_cast<const uint8_t*>(a.s);
-            const uint8_t* bbase = reinterpret_cast<const uint8_t*>(a.b);
             for (int r = lane; r < nf * 16; r += 32) {
-                const int grow = row0 + r;
+                const int fi = r >> 4;
+                int frow_r = frow[0], fmat_r = fmat[0];
+#pragma unroll
+                for (int i = 1; i < FR; ++i)
+                    if (fi == i) {
+                        frow_r = frow[i];
+                        fmat_r = fmat[i];
+                    }
+                const int grow = frow_r + (r & 15);
+                const uint8_t* sbase = reinterpret_cast<const uint8_t*>(fmat_r ? a.s1 : a.s);
+                const uint8_t* bbase = reinterpret_cast<const uint8_t*>(fmat_r ? a.b1 : a.b);
                 for (int u = 0; u < units; ++u) {
                     const int gcol = 8 * c + u * (vb >> 1);
                     const bool valid = grow < a.N && gcol < a.kg;
@@ -208,17 +297,27 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
             for (int e = 0; e < 4; ++e) acc[f][q][e] = 0.0f;
 
     // this lane's 8 bytes of a row inside group w of a stage (128-byte swizzle: 16-byte chunk c of row r sits at
-    // c ^ (r & 7)); the stage's box is [segment][16 nf rows][128 bytes], fragment f's rows at 2048 f of each segment
-    const uint32_t w_off = (warp >> 2) * (nf * 2048) + g * 128 + (((2 * (warp & 3) + (t >> 1)) ^ g) << 4) + 8 * (t & 1);
-    // x of stage i's group for this lane: values 16t .. 16t + 15 of tokens g + 8 mt (zero past M and past K)
+    // c ^ (r & 7)); dense: the stage's box is [segment][16 nf rows][128 bytes], fragment f's rows at 2048 f of each
+    // segment; MoE: fragment f's own box [segment][16 rows][128 bytes] at 4096 f
+    const uint32_t frag_stride = moe ? S::W_FRAG : 2048;
+    const uint32_t w_off = (warp >> 2) * (moe ? 2048 : nf * 2048) + g * 128 + (((2 * (warp & 3) + (t >> 1)) ^ g) << 4) +
+                           8 * (t & 1);
+    // x of stage i's group for this lane: values 16t .. 16t + 15 of tokens g + 8 mt (zero past M and past K); the fused
+    // down + combine puts slot g's row of h (pos[g]) in token column g
     const uint8_t* xg = reinterpret_cast<const uint8_t*>(a.x);
+    int xrow[MT];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+        const int tok = 8 * mt + g;
+        xrow[mt] = (a.mode == QG_MOE_COMBINE && a.pos && tok < a.M) ? a.pos[tok] : tok;
+    }
     auto fetch_x = [&](int i, uint4 (&u)[MT][2]) {
         const int gi = 8 * i + warp;
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
             const int tok = 8 * mt + g;
             if (tok < a.M && gi < a.kg) {
-                const uint4* p = reinterpret_cast<const uint4*>(xg + (size_t(tok) * a.K + gi * 64 + 16 * t) * 2);
+                const uint4* p = reinterpret_cast<const uint4*>(xg + (size_t(xrow[mt]) * a.K + gi * 64 + 16 * t) * 2);
                 u[mt][0] = p[0];
                 u[mt][1] = p[1];
             } else {
@@ -260,7 +359,7 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
 #pragma unroll
             for (int f = 0; f < FR; ++f) {
                 {
-                    const uint32_t fb = st + f * 2048 + w_off;
+                    const uint32_t fb = st + f * frag_stride + w_off;
                     const uint2 wa = qg_lds64(fb), wb = qg_lds64(fb + 8 * 128);
                     const int ra = 16 * f + g, rb = ra + 8;
                     const uint32_t sa = lds_u16(sb + ra * 16), ba = lds_u16(sb + S::SB_BYTES + ra * 16);
@@ -308,14 +407,42 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
                 red[(warp * S::MTOK + tok) * RR + row] = acc[f][mt][e];
             }
     named_barrier(1, 32 * QG_CW);
+    auto sum_warps = [&](int tok, int row) {
+        float v = 0.0f;
+#pragma unroll
+        for (int w = 0; w < QG_CW; ++w) v += red[(w * S::MTOK + tok) * RR + row];
+        return v;
+    };
+    if (a.mode == QG_MOE_GLU) {
+        // unit i: gate rows at fragment 2i, up rows at 2i + 1 -> h[segment][16 fe + r]
+        for (int idx = threadIdx.x; idx < nu * 16; idx += 32 * QG_CW) {
+            const int i = idx >> 4, r = idx & 15;
+            const int u = u0 + i, seg = u / a.fpe, fe = u - seg * a.fpe;
+            const float v = qg_swiglu<T>(sum_warps(0, 32 * i + r), sum_warps(0, 32 * i + 16 + r));
+            if (ok) qg_store(a, seg, 16 * fe + r, v, kBF16);
+        }
+        return;
+    }
+    if (a.mode == QG_MOE_COMBINE) {
+        // unit i: slot r's rows at fragment k i + r, its token column r; y = sum_r w_r * round(y_r), slots in order
+        const int k = a.fpu;
+        for (int idx = threadIdx.x; idx < nu * 16; idx += 32 * QG_CW) {
+            const int i = idx >> 4, r = idx & 15;
+            float y = 0.0f;
+            for (int sl = 0; sl < k; ++sl) {
+                const float ys = qg_round<T>(sum_warps(sl, 16 * (k * i + sl) + r));
+                y = fmaf(ys, a.wts[sl], y);  // as the stand-alone combine kernel sums the slots
+            }
+            if (ok) qg_store(a, 0, 16 * (u0 + i) + r, y, kBF16);
+        }
+        return;
+    }
     const int R = nf * 16;
     for (int idx = threadIdx.x; idx < R * mv; idx += 32 * QG_CW) {
         const int tok = idx / R, row = idx - tok * R;
         const int n = row0 + row;
         if (n >= a.N) continue;
-        float v = 0.0f;
-#pragma unroll
-        for (int w = 0; w < QG_CW; ++w) v += red[(w * S::MTOK + tok) * RR + row];
+        const float v = sum_warps(tok, row);
         if (ok) qg_store(a, tok, n, v, kBF16);
     }
 }
@@ -325,7 +452,8 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
 // ------------------------------------------------------------------------------------------------
 
 template <typename T, int MT, int FR>
-static int qmvg_launch_t(const void* x, const uint32_t* w, QgArgs a, int ns_req, int nctas, cudaStream_t st) {
+static int qmvg_launch_t(const void* x, const uint32_t* w, const uint32_t* w1, QgArgs a, int ns_req, int nctas,
+                         cudaStream_t st) {
     using S = QgShape<MT, FR>;
     const DeviceInfo& di = device_info();
     const int K = a.K;
@@ -343,20 +471,24 @@ static int qmvg_launch_t(const void* x, const uint32_t* w, QgArgs a, int ns_req,
     const size_t smem = ring + fixed;
     if (smem > di.smem_optin) return LQ_E_SHAPE;
 
-    // weight boxes of 16 FR rows (CTAs holding FR fragments) and 16 (FR - 1) rows (the others), two segments a stage
+    // dense: weight boxes of 16 FR rows (CTAs holding FR fragments) and 16 (FR - 1) rows (the others); MoE: 16-row
+    // boxes of the two stacked matrices (gate / up, or down twice); two 128-byte segments a stage
+    const bool moe = a.mode != QG_DENSE;
     CUtensorMap tw[2];
     for (int m = 0; m < 2; ++m) {
-        const int rows = 16 * (m == 0 || FR == 1 ? FR : FR - 1);
+        const int rows = moe ? 16 : 16 * (m == 0 || FR == 1 ? FR : FR - 1);
         const uint64_t dims[3] = {32, uint64_t(a.N), uint64_t(K) / 256};
         const uint64_t str[2] = {uint64_t(K) / 2, 128};
         const uint32_t box[3] = {32, uint32_t(rows), 2};
+        const uint32_t* base = (moe && m == 1 && w1) ? w1 : w;
         const int rc =
-            make_tmap(&tw[m], CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, w, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+            make_tmap(&tw[m], CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, base, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
     }
     a.x = x;
     const int kg = a.kg;
-    const uintptr_t sb_addr = reinterpret_cast<uintptr_t>(a.s) | reinterpret_cast<uintptr_t>(a.b);
+    const uintptr_t sb_addr = reinterpret_cast<uintptr_t>(a.s) | reinterpret_cast<uintptr_t>(a.b) |
+                              reinterpret_cast<uintptr_t>(a.s1) | reinterpret_cast<uintptr_t>(a.b1);
     a.sb_vec = (kg % 8 == 0 && sb_addr % 16 == 0) ? 16 : (kg % 4 == 0 && sb_addr % 8 == 0) ? 8 : 4;
 
     auto kern = qmvg_kernel<T, MT, FR>;
@@ -377,13 +509,13 @@ static int qmvg_launch_t(const void* x, const uint32_t* w, QgArgs a, int ns_req,
 }
 
 template <typename T, int MT>
-static int qmvg_dispatch_fr(int FR, const void* x, const uint32_t* w, const QgArgs& a, int ns, int nctas,
-                            cudaStream_t st) {
+static int qmvg_dispatch_fr(int FR, const void* x, const uint32_t* w, const uint32_t* w1, const QgArgs& a, int ns,
+                            int nctas, cudaStream_t st) {
     switch (FR) {
-        case 1: return qmvg_launch_t<T, MT, 1>(x, w, a, ns, nctas, st);
-        case 2: return qmvg_launch_t<T, MT, 2>(x, w, a, ns, nctas, st);
-        case 3: return qmvg_launch_t<T, MT, 3>(x, w, a, ns, nctas, st);
-        case 4: return qmvg_launch_t<T, MT, 4>(x, w, a, ns, nctas, st);
+        case 1: return qmvg_launch_t<T, MT, 1>(x, w, w1, a, ns, nctas, st);
+        case 2: return qmvg_launch_t<T, MT, 2>(x, w, w1, a, ns, nctas, st);
+        case 3: return qmvg_launch_t<T, MT, 3>(x, w, w1, a, ns, nctas, st);
+        case 4: return qmvg_launch_t<T, MT, 4>(x, w, w1, a, ns, nctas, st);
         default: return LQ_E_SHAPE;
     }
 }
@@ -423,12 +555,68 @@ int qmvg_run(const void* x, const uint32_t* w, const void* s, const void* b, int
     int nctas = (a.nfrag + fr - 1) / fr;
     if (fr_req == 0 && nctas < sms) nctas = a.nfrag < sms ? a.nfrag : sms;
     const int FR = (a.nfrag + nctas - 1) / nctas;
+    a.mode = QG_DENSE;
+    a.fpu = 1;
+    a.units = a.nfrag;
     const bool bf16 = dtype == LQ_BF16;
     if (M <= 8)
-        return bf16 ? qmvg_dispatch_fr<__nv_bfloat16, 1>(FR, x, w, a, ns, nctas, st)
-                    : qmvg_dispatch_fr<__half, 1>(FR, x, w, a, ns, nctas, st);
-    return bf16 ? qmvg_dispatch_fr<__nv_bfloat16, 2>(FR, x, w, a, ns, nctas, st)
-                : qmvg_dispatch_fr<__half, 2>(FR, x, w, a, ns, nctas, st);
+        return bf16 ? qmvg_dispatch_fr<__nv_bfloat16, 1>(FR, x, w, nullptr, a, ns, nctas, st)
+                    : qmvg_dispatch_fr<__half, 1>(FR, x, w, nullptr, a, ns, nctas, st);
+    return bf16 ? qmvg_dispatch_fr<__nv_bfloat16, 2>(FR, x, w, nullptr, a, ns, nctas, st)
+                : qmvg_dispatch_fr<__half, 2>(FR, x, w, nullptr, a, ns, nctas, st);
+}
+
+// The MoE decode modes for ONE token (its k pairs, one a segment of the grouping) over stacked (E, rows_e, K) 4-bit
+// experts. glu: out (k, rows_e) = swiglu(x . gate_e^T, x . up_e^T) of segment s's expert experts[s], rows in segment
+// order. combine (k <= 4): out (1, rows_e) = sum_r wts[r] * round(h[pos[r]] . down_e^T), e = experts[pos[r]], slots in
+// order. 0 or LQ_E_SHAPE when the shape does not fit these modes (the caller then uses the grouped qmv path).
+bool qmvg_moe_ok(int mode, int k, int rows_e, int K, int sms) {
+    if (k < 1 || k > 8 || rows_e < 16 || rows_e % 16 || K < 256 || K % 256) return false;
+    const int fpe = rows_e / 16;
+    if (mode == QG_MOE_GLU) return (k * fpe + sms - 1) / sms * 2 <= QG_MAX_FR;
+    return k <= QG_MAX_FR;
+}
+
+int qmvg_moe_run(int mode, const void* x, const int32_t* experts, const int32_t* pos, const float* wts,
+                 const uint32_t* w0, const void* s0, const void* b0, const uint32_t* w1, const void* s1, const void* b1,
+                 void* out, int k, int E, int rows_e, int K, int dtype, cudaStream_t st) {
+    const int sms = device_info().sm_count;
+    if (!qmvg_moe_ok(mode, k, rows_e, K, sms)) return LQ_E_SHAPE;
+    QgArgs a = {};
+    a.mode = mode;
+    a.K = K;
+    a.kg = K / 64;
+    a.nchunk = (K + 511) / 512;
+    a.N = E * rows_e;  // rows of each stack
+    a.rows_e = rows_e;
+    a.fpe = rows_e / 16;
+    a.experts = experts;
+    a.pos = pos;
+    a.wts = wts;
+    a.s = s0;
+    a.b = b0;
+    a.s1 = mode == QG_MOE_GLU ? s1 : s0;
+    a.b1 = mode == QG_MOE_GLU ? b1 : b0;
+    a.out[0] = out;
+    a.ldo[0] = rows_e;
+    a.seg_end[0] = rows_e;
+    a.nseg_out = 1;
+    if (mode == QG_MOE_GLU) {
+        a.M = 1;  // the one token
+        a.fpu = 2;
+        a.units = k * a.fpe;
+    } else {
+        a.M = k;  // slot r's row of h in token column r
+        a.fpu = k;
+        a.units = a.fpe;
+    }
+    a.nfrag = a.units * a.fpu;
+    const int nctas = a.units < sms ? a.units : sms;
+    const int FR = (a.units + nctas - 1) / nctas * a.fpu;
+    const bool bf16 = dtype == LQ_BF16;
+    const uint32_t* wm1 = mode == QG_MOE_GLU ? w1 : w0;
+    return bf16 ? qmvg_dispatch_fr<__nv_bfloat16, 1>(FR, x, w0, wm1, a, 0, nctas, st)
+                : qmvg_dispatch_fr<__half, 1>(FR, x, w0, wm1, a, 0, nctas, st);
 }
 
 }  // namespace lq

@@ -42,10 +42,10 @@
 
 namespace lq {
 
-template <typename T, int BITS, int NMAT, int NTOK>
+template <typename T, int BITS, int NMAT, int NTOK, bool FULL>
 __device__ __forceinline__ void tcv_body(const CUtensorMap& tm_w0, const CUtensorMap& tm_w1, const CUtensorMap& tm_x,
                                          const TcvArgs& a) {
-    using S = TcvShape<BITS, NMAT, NTOK>;
+    using S = TcvShape<BITS, NMAT, NTOK, FULL>;
     constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -356,22 +356,24 @@ template <typename T, int BITS, int NMAT, int NTOK>
 __global__ void __maxnreg__(64)
     tcv_kernel_dec(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
                    const __grid_constant__ CUtensorMap tm_x, const TcvArgs a) {
-    tcv_body<T, BITS, NMAT, NTOK>(tm_w0, tm_w1, tm_x, a);
+    tcv_body<T, BITS, NMAT, NTOK, false>(tm_w0, tm_w1, tm_x, a);
 }
 
-template <typename T, int BITS, int NMAT, int NTOK>
+// Wide tiles (prefill), and decode tiles in the FULL form (all of an SM's tensor memory, registers and shared memory:
+// one CTA per SM and no room for the next launch's CTA, for weights large enough to keep the SM streaming alone).
+template <typename T, int BITS, int NMAT, int NTOK, bool FULL>
 __global__ void __launch_bounds__(TCV_THREADS, 1)
     tcv_kernel_wide(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
                     const __grid_constant__ CUtensorMap tm_x, const TcvArgs a) {
-    tcv_body<T, BITS, NMAT, NTOK>(tm_w0, tm_w1, tm_x, a);
+    tcv_body<T, BITS, NMAT, NTOK, FULL>(tm_w0, tm_w1, tm_x, a);
 }
 
 // ------------------------------------------------------------------------------------------------
 
-template <typename T, int BITS, int NMAT, int NTOK>
+template <typename T, int BITS, int NMAT, int NTOK, bool FULL>
 static int tcv_launch_t(const void* x, int x_rows, const QmvMats& mats, TcvArgs a, int ks, int ws_req, int gz,
                         cudaStream_t st) {
-    using S = TcvShape<BITS, NMAT, NTOK>;
+    using S = TcvShape<BITS, NMAT, NTOK, FULL>;
     const DeviceInfo& di = device_info();
     const int pairs = a.G / 2;
     if (ks < 1) ks = 1;
@@ -382,7 +384,7 @@ static int tcv_launch_t(const void* x, int x_rows, const QmvMats& mats, TcvArgs 
     a.sbw = (gc_max / 2) | 1;
     const size_t sb_bytes = size_t(NMAT) * 2 * 128 * a.sbw * 4;
     const size_t bar_bytes = (4 * TCV_MAX_SLOTS + 2 * S::AS + 1) * 8 + 16;
-    size_t budget = NTOK <= 64 ? di.smem_per_sm / 2 - 2048 : di.smem_optin - 1024;
+    size_t budget = (NTOK <= 64 && !FULL) ? di.smem_per_sm / 2 - 2048 : di.smem_optin - 1024;
     const int nw_max = (gc_max + S::WG - 1) / S::WG;
     int ws = nw_max < TCV_MAX_SLOTS ? nw_max : TCV_MAX_SLOTS;
     int xs = gc_max < TCV_MAX_SLOTS ? gc_max : TCV_MAX_SLOTS;
@@ -438,10 +440,10 @@ static int tcv_launch_t(const void* x, int x_rows, const QmvMats& mats, TcvArgs 
     }
 
     void (*kern)(CUtensorMap, CUtensorMap, CUtensorMap, TcvArgs);
-    if constexpr (NTOK <= 64)
+    if constexpr (NTOK <= 64 && !FULL)
         kern = tcv_kernel_dec<T, BITS, NMAT, NTOK>;
     else
-        kern = tcv_kernel_wide<T, BITS, NMAT, NTOK>;
+        kern = tcv_kernel_wide<T, BITS, NMAT, NTOK, FULL>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return LQ_E_CUDA;
     cudaLaunchConfig_t cfg = {};
@@ -468,33 +470,39 @@ static int tcv_launch_t(const void* x, int x_rows, const QmvMats& mats, TcvArgs 
 }
 
 template <typename T, int BITS, int NMAT>
-static int tcv_dispatch_tok(int ntok, const void* x, int x_rows, const QmvMats& mats, const TcvArgs& a, int ks, int ws,
-                            int gz, cudaStream_t st) {
-    if (ntok == 16) return tcv_launch_t<T, BITS, NMAT, 16>(x, x_rows, mats, a, ks, ws, gz, st);
-    if (ntok == 32) return tcv_launch_t<T, BITS, NMAT, 32>(x, x_rows, mats, a, ks, ws, gz, st);
-    if (ntok == 64) return tcv_launch_t<T, BITS, NMAT, 64>(x, x_rows, mats, a, ks, ws, gz, st);
-    if (ntok == 128) return tcv_launch_t<T, BITS, NMAT, 128>(x, x_rows, mats, a, ks, ws, gz, st);
+static int tcv_dispatch_tok(int ntok, bool full, const void* x, int x_rows, const QmvMats& mats, const TcvArgs& a,
+                            int ks, int ws, int gz, cudaStream_t st) {
+    if (ntok == 16)
+        return full ? tcv_launch_t<T, BITS, NMAT, 16, true>(x, x_rows, mats, a, ks, ws, gz, st)
+                    : tcv_launch_t<T, BITS, NMAT, 16, false>(x, x_rows, mats, a, ks, ws, gz, st);
+    if (ntok == 32)
+        return full ? tcv_launch_t<T, BITS, NMAT, 32, true>(x, x_rows, mats, a, ks, ws, gz, st)
+                    : tcv_launch_t<T, BITS, NMAT, 32, false>(x, x_rows, mats, a, ks, ws, gz, st);
+    if (ntok == 64)
+        return full ? tcv_launch_t<T, BITS, NMAT, 64, true>(x, x_rows, mats, a, ks, ws, gz, st)
+                    : tcv_launch_t<T, BITS, NMAT, 64, false>(x, x_rows, mats, a, ks, ws, gz, st);
+    if (ntok == 128) return tcv_launch_t<T, BITS, NMAT, 128, false>(x, x_rows, mats, a, ks, ws, gz, st);
     if constexpr (NMAT == 1) {
-        if (ntok == 256) return tcv_launch_t<T, BITS, NMAT, 256>(x, x_rows, mats, a, ks, ws, gz, st);
+        if (ntok == 256) return tcv_launch_t<T, BITS, NMAT, 256, false>(x, x_rows, mats, a, ks, ws, gz, st);
     }
     return LQ_E_UNSUPPORTED;
 }
 
 static int tcv_dispatch(const void* x, int x_rows, const QmvMats& mats, int nmat, const TcvArgs& a, int bits, int dtype,
-                        int ntok, int ks, int ws, int gz, cudaStream_t st) {
+                        int ntok, bool full, int ks, int ws, int gz, cudaStream_t st) {
     const bool bf16 = dtype == LQ_BF16;
     if (bits == 4) {
         if (nmat == 1)
-            return bf16 ? tcv_dispatch_tok<__nv_bfloat16, 4, 1>(ntok, x, x_rows, mats, a, ks, ws, gz, st)
-                        : tcv_dispatch_tok<__half, 4, 1>(ntok, x, x_rows, mats, a, ks, ws, gz, st);
-        return bf16 ? tcv_dispatch_tok<__nv_bfloat16, 4, 2>(ntok, x, x_rows, mats, a, ks, ws, gz, st)
-                    : tcv_dispatch_tok<__half, 4, 2>(ntok, x, x_rows, mats, a, ks, ws, gz, st);
+            return bf16 ? tcv_dispatch_tok<__nv_bfloat16, 4, 1>(ntok, full, x, x_rows, mats, a, ks, ws, gz, st)
+                        : tcv_dispatch_tok<__half, 4, 1>(ntok, full, x, x_rows, mats, a, ks, ws, gz, st);
+        return bf16 ? tcv_dispatch_tok<__nv_bfloat16, 4, 2>(ntok, full, x, x_rows, mats, a, ks, ws, gz, st)
+                    : tcv_dispatch_tok<__half, 4, 2>(ntok, full, x, x_rows, mats, a, ks, ws, gz, st);
     }
     if (nmat == 1)
-        return bf16 ? tcv_dispatch_tok<__nv_bfloat16, 8, 1>(ntok, x, x_rows, mats, a, ks, ws, gz, st)
-                    : tcv_dispatch_tok<__half, 8, 1>(ntok, x, x_rows, mats, a, ks, ws, gz, st);
-    return bf16 ? tcv_dispatch_tok<__nv_bfloat16, 8, 2>(ntok, x, x_rows, mats, a, ks, ws, gz, st)
-                : tcv_dispatch_tok<__half, 8, 2>(ntok, x, x_rows, mats, a, ks, ws, gz, st);
+        return bf16 ? tcv_dispatch_tok<__nv_bfloat16, 8, 1>(ntok, full, x, x_rows, mats, a, ks, ws, gz, st)
+                    : tcv_dispatch_tok<__half, 8, 1>(ntok, full, x, x_rows, mats, a, ks, ws, gz, st);
+    return bf16 ? tcv_dispatch_tok<__nv_bfloat16, 8, 2>(ntok, full, x, x_rows, mats, a, ks, ws, gz, st)
+                : tcv_dispatch_tok<__half, 8, 2>(ntok, full, x, x_rows, mats, a, ks, ws, gz, st);
 }
 
 // K slices for rb row tiles: about 1.3 CTAs per SM in total (measured on B200 over the fused QKV,
@@ -515,7 +523,7 @@ bool tcv_shape_ok(int M, int K, int bits) {
     return bits == 4 || bits == 8;
 }
 
-// p = {NTOK, KS, WS} (0 = choose).
+// p = {NTOK, KS, WS, FORM} (0 = choose; FORM 2 = the full-SM form of a decode tile).
 int tcv_run(const void* x, int M, const QmvMats& mats, int nmat, int N, int K, int nout, void* const* outs,
             const int* seg_end, const int* ldo, int bits, int dtype, const int* p, cudaStream_t st) {
     if (!tcv_shape_ok(M, K, bits)) return LQ_E_SHAPE;
@@ -534,7 +542,8 @@ int tcv_run(const void* x, int M, const QmvMats& mats, int nmat, int N, int K, i
     if (ntok == 0) ntok = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 || nmat == 2 ? 128 : 256;
     if (ntok != 16 && ntok != 32 && ntok != 64 && ntok != 128 && ntok != 256) return LQ_E_ARG;
     if (ks == 0) ks = tcv_default_ks((N + 127) / 128 * ((M + ntok - 1) / ntok), a.G / 2, device_info().sm_count);
-    return tcv_dispatch(x, M, mats, nmat, a, bits, dtype, ntok, ks, ws, 0, st);
+    const bool full = p && p[3] == 2 && ntok <= 64;
+    return tcv_dispatch(x, M, mats, nmat, a, bits, dtype, ntok, full, ks, ws, 0, st);
 }
 
 // Grouped expert GEMMs (the MoE path): x = the expert-sorted rows xs (P rows), weights stacked (E, N, ...).
@@ -564,7 +573,7 @@ int tcv_run_grouped(const void* xs, int P, const QmvMats& mats, int nmat, int N,
     if (ntok != 16 && ntok != 32 && ntok != 64) return LQ_E_ARG;
     // tiles: at most one partial tile per used expert plus P / ntok full ones
     const int gz = used + (P + ntok - 1) / ntok;
-    return tcv_dispatch(xs, P, mats, nmat, a, bits, dtype, ntok, 1, p ? p[2] : 0, gz, st);
+    return tcv_dispatch(xs, P, mats, nmat, a, bits, dtype, ntok, false, 1, p ? p[2] : 0, gz, st);
 }
 
 }  // namespace lq

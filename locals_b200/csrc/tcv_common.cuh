@@ -44,7 +44,7 @@ struct TcvArgs {
     int n_experts;
 };
 
-template <int BITS, int NMAT, int NTOK>
+template <int BITS, int NMAT, int NTOK, bool FULL = false>
 struct TcvShape {
     static constexpr int GB = BITS * 8;     // bytes of one row of one group: 32 (4-bit) or 64 (8-bit)
     static constexpr int GW = GB / 4;       // uint32 words of one row of one group
@@ -54,7 +54,9 @@ struct TcvShape {
     // MMA issuers = accumulators: small-N MMAs are bound by the issue rate of one thread (~24 ns each on
     // B200), so narrow token tiles spread them over several issuing warps; a multiple of NMAT
     static constexpr int NACC = NTOK <= 16 ? 4 : (NTOK <= 64 || NMAT == 2) ? 2 : 1;
-    static constexpr int TMEM_COLS = NTOK <= 64 ? 256 : 512;
+    // decode tiles keep half the tensor memory so the next launch's CTA can work beside this one; FULL (one CTA per SM,
+    // for weights large enough to keep the SM streaming on their own) and wide tiles take all 512 columns
+    static constexpr int TMEM_COLS = (NTOK <= 64 && !FULL) ? 256 : 512;
     static constexpr int DCOLS = NACC * NTOK;
     static constexpr int AS = (TMEM_COLS - DCOLS) / 32;  // tensor-memory A ring, one group (32 columns) each
     static_assert(AS >= 2 && DCOLS + 32 * AS <= TMEM_COLS, "accumulators and A ring exceed the TMEM allocation");

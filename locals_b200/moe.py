@@ -115,6 +115,28 @@ def experts(xs: torch.Tensor, grouping, mats: Sequence, N: int, max_rows: int, b
     return out
 
 
+def down_combine(h: torch.Tensor, grouping, weights: torch.Tensor, down, bits: int = 4,
+                 group_size: int = 64) -> Optional[torch.Tensor]:
+    """One token's down projections and the weighted combine of its k slots in one kernel (lq_moe_down_combine):
+    y (1, D), or None when the shape is outside the fused kernel (use experts + combine then)."""
+    k = weights.shape[-1]
+    if weights.numel() != k or bits != 4:
+        return None
+    _, _, experts_, _, pos = grouping
+    w, s, b = down
+    E, N = w.shape[0], w.shape[1]
+    K = h.shape[-1]
+    y = torch.empty((1, N), dtype=h.dtype, device=h.device)
+    rc = _lib.lib().lq_moe_down_combine(h.data_ptr(), experts_.data_ptr(), None if pos is None else pos.data_ptr(),
+                                        weights.data_ptr(), w.data_ptr(), s.data_ptr(), b.data_ptr(), y.data_ptr(), k,
+                                        E, N, K, bits, group_size, dtype_code(h.dtype), _stream())
+    if rc == _lib.LQ_E_SHAPE:
+        return None
+    if rc != _lib.LQ_OK:
+        raise _lib.LQError("lq_moe_down_combine", rc)
+    return y
+
+
 def combine(ys: torch.Tensor, weights: torch.Tensor, pos: Optional[torch.Tensor]) -> torch.Tensor:
     T, k = weights.shape
     D = ys.shape[-1]
@@ -206,5 +228,15 @@ class MoELayer:
         x2 = x.reshape(-1, D).contiguous()
         inds, wts = self.route(x2)
         grouping = direct_grouping(inds) if x2.shape[0] <= DIRECT_MAX_TOKENS else group(inds, self.n_experts)
+        if x2.shape[0] == 1:  # one token: the down projections and the combine in one kernel
+            M, k = inds.shape
+            h = experts(x2, grouping, [self.gate, self.up], self.gate[0].shape[1], max_rows=M, bits=self.bits,
+                        group_size=self.group_size, gather_k=k)
+            y = down_combine(h, grouping, wts, self.down, self.bits, self.group_size)
+            if y is not None:
+                return y.reshape(x.shape)
+            ys = experts(h, grouping, [self.down], self.down[0].shape[1], max_rows=M, bits=self.bits,
+                         group_size=self.group_size)
+            return combine(ys, wts, grouping[4]).reshape(x.shape)
         ys = switch_glu_grouped(x2, inds, self.gate, self.up, self.down, self.bits, self.group_size, grouping)
         return combine(ys, wts, grouping[4]).reshape(x.shape)
