@@ -203,11 +203,12 @@ def test_merge_keeps_both_processes_crash_counts_and_shared_stale_keys():
 def test_an_idle_tuner_leaves_its_shapes_while_another_process_is_busy(cache, monkeypatch):
     busy = cache.parent / "busy"
     busy.mkdir()
-    other = busy / f"busy-{os.getppid()}"
-    other.write_text("")
     dead = busy / f"busy-{_dead_pid()}"
     dead.write_text("")
-    assert tune.others_busy() and not dead.exists()
+    assert not tune.others_busy() and not dead.exists()  # a dead process's heartbeat goes
+    other = busy / f"busy-{os.getppid()}"
+    other.write_text("")
+    assert tune.others_busy()
     key = "2560x4096x8xbfloat16"
     cache.write_text(json.dumps({key: ["qmv", 1, 2, 1, 0], "__lib__": "v1"}))
     monkeypatch.setattr(tune, "_time_shape", lambda *a: (("qmvg", 0, 0), 0.01))
