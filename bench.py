@@ -211,8 +211,9 @@ def capture(torch, body, stream):
     return g
 
 
-def bench_qkv(torch, M, layers, steps, warmup, dev, stream, with_e2e=False):
-    """Fused QKV (config 2) over `layers` distinct weight copies; returns a dict of measurements."""
+def bench_qkv(torch, M, layers, steps, warmup, dev, stream, with_e2e=False, choice=None):
+    """Fused QKV (config 2) over `layers` distinct weight copies; returns a dict of measurements. `choice` pins a
+    kernel family (None: the library's own choice)."""
     from locals_b200 import kernels
 
     gen = torch.Generator(device=dev)
@@ -223,7 +224,7 @@ def bench_qkv(torch, M, layers, steps, warmup, dev, stream, with_e2e=False):
 
     def body():
         for i, (w, s, b) in enumerate(Ws):
-            outs["qkv"] = kernels.qmm_split(x, w, s, b, HEAD_WIDTHS)
+            outs["qkv"] = kernels.qmm_split(x, w, s, b, HEAD_WIDTHS, choice=choice)
 
     g = capture(torch, body, stream)
     ms = timed(torch, g.replay, steps, warmup, stream)
@@ -515,6 +516,13 @@ def run_gpu(args):
             r = bench_qkv(torch, M, head_layers, max(5, args.steps // 2), args.warmup, dev, stream)
             extra["cfg2_fused_qkv"][f"M={M}"] = {"GB/s": round(r["gbs"], 1), "frac_hbm": round(r["gbs"] / hbm, 3),
                                                  "us_per_call": round(r["us_per_launch"], 3)}
+        # the two 4-bit decode families on the headline shape (the library's choice is one of them)
+        extra["cfg2_decode_families_us"] = {}
+        for fam in ("qmvg", "qmvq"):
+            for M in (1, 4, 8, 16):
+                r = bench_qkv(torch, M, head_layers, max(5, args.steps // 2), args.warmup, dev, stream,
+                              choice=(fam, 0, 0))
+                extra["cfg2_decode_families_us"][f"{fam} M={M}"] = round(r["us_per_launch"], 3)
         r = bench_cfg1(torch, max(5, args.steps // 2), args.warmup, dev, stream)
         extra["cfg1_qmm_fp16_m8"] = {"GB/s": round(r["gbs"], 1), "frac_hbm": round(r["gbs"] / hbm, 3),
                                      "us_per_call": round(r["us_per_call"], 3)}

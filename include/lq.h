@@ -36,11 +36,15 @@ extern "C" {
 
 /* Kernel families, the analogue of the reference's tuning choices (locals/kernels.py:136-144). */
 #define LQ_FAM_AUTO 0   /* pick by shape: TC from 65 rows; TCV for 33-64 rows or >= 24 MB of weights from 9 rows;
-                           QMVG for 1-4 rows of a 4-bit matrix (K % 256 == 0); else QMV */
+                           QMVQ for 1-8 rows of a 4-bit matrix with K <= 4096 (K % 256 == 0) and 9-16 rows with
+                           K <= 2560, N <= 8192; else QMV */
 #define LQ_FAM_QMV 1    /* decode: TMA-staged packed weights, register dequant, mma.sync; p = {MT, WK, KS, NS} */
 #define LQ_FAM_TC 2     /* prefill: dequant tiles into shared memory, tcgen05.mma into TMEM */
 #define LQ_FAM_TCV 3    /* tcgen05 with weights dequantized into TMEM (A operand), tokens as N;
                            p = {NTOK, KS, WS, PERSISTENT (1: one CTA per SM walks the tiles)} */
+#define LQ_FAM_QMVQ 5   /* as QMVG, with the codes fed raw to the MMA (128 + q / 1024 + q) and each group's scale and
+                           bias folded in fp32 (y += s acc + (b - magic s) sum x), the weights never rounded to the
+                           activation dtype: the reference's fragq formulation; p = {FR, NS} */
 #define LQ_FAM_QMVG 4   /* dense 4-bit decode, M <= 16, K % 256 == 0: each warp takes one 64-wide group of every
                            stage for all of its CTA's 16-row fragments, fragments spread over every SM;
                            p = {FR (max fragments a CTA, <= 4), NS} */

@@ -12,7 +12,7 @@ LIB_PATH = os.path.join(HERE, "liblq.so")
 
 LQ_OK, LQ_E_ARG, LQ_E_SHAPE, LQ_E_ALIGN, LQ_E_UNSUPPORTED, LQ_E_CUDA, LQ_E_DEVICE, LQ_E_SCRATCH = range(8)
 F16, BF16, F32 = 0, 1, 2
-FAM_AUTO, FAM_QMV, FAM_TC, FAM_TCV, FAM_QMVG = 0, 1, 2, 3, 4
+FAM_AUTO, FAM_QMV, FAM_TC, FAM_TCV, FAM_QMVG, FAM_QMVQ = 0, 1, 2, 3, 4, 5
 
 # every function the header declares, with its argument types (checked by tests on CPU)
 _vp, _i, _u32p = ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p

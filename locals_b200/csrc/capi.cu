@@ -47,6 +47,9 @@ int qmm_dense_run(const void* x, const uint32_t* w, const void* s, const void* b
 bool qmvg_shape_ok(int M, int K, int bits);
 int qmvg_run(const void* x, const uint32_t* w, const void* s, const void* b, int nout, void* const* outs,
              const int* seg_end, const int* ldo, int M, int N, int K, int dtype, const int* p, cudaStream_t st);
+bool qmvq_shape_ok(int M, int K, int bits);
+int qmvq_run(const void* x, const uint32_t* w, const void* s, const void* b, int nout, void* const* outs,
+             const int* seg_end, const int* ldo, int M, int N, int K, int dtype, const int* p, cudaStream_t st);
 bool qmvg_moe_ok(int mode, int k, int rows_e, int K, int sms);
 int qmvg_moe_run(int mode, const void* x, const int32_t* experts, const int32_t* pos, const float* wts,
                  const uint32_t* w0, const void* s0, const void* b0, const uint32_t* w1, const void* s1, const void* b1,
@@ -125,6 +128,10 @@ static int qmm_common(const void* x, const uint32_t* w, const void* s, const voi
         if (!tc_shape_ok(M, N, K, bits)) return LQ_E_SHAPE;
         return finish(tc_run(x, w, s, b, outs[0], M, N, K, bits, dtype, cfg ? cfg->p : nullptr, st));
     }
+    if (fam == LQ_FAM_QMVQ) {
+        if (!qmvq_shape_ok(M, K, bits)) return LQ_E_SHAPE;
+        return finish(qmvq_run(x, w, s, b, nout, outs, a.seg_end, a.ldo, M, N, K, dtype, cfg->p, st));
+    }
     if (fam == LQ_FAM_QMVG) {
         if (!qmvg_shape_ok(M, K, bits)) return LQ_E_SHAPE;
         return finish(qmvg_run(x, w, s, b, nout, outs, a.seg_end, a.ldo, M, N, K, dtype, cfg->p, st));
@@ -142,12 +149,16 @@ static int qmm_common(const void* x, const uint32_t* w, const void* s, const voi
         rc = tcv_run(x, M, mats, 1, N, K, nout, outs, a.seg_end, a.ldo, bits, dtype, nullptr, st);
         if (rc != LQ_E_SHAPE) return finish(rc);
     }
-    // 1-16 tokens of a 4-bit matrix: the group-per-warp family, measured faster than qmv on the fused QKV projection
-    // at every token count (B200, CUDA graph of 36 layers, us a layer: 5.09 vs 6.04 at M=1, 5.49 vs 5.93 at M=8,
-    // 6.73 vs 7.06 at M=16); qmv for the other shapes
-    if (fam == LQ_FAM_AUTO && qmvg_shape_ok(M, K, bits)) {
-        const int p[2] = {0, 0};
-        rc = qmvg_run(x, w, s, b, nout, outs, a.seg_end, a.ldo, M, N, K, dtype, p, st);
+    // Few tokens of a 4-bit matrix: the folded group-per-warp family (codes fed raw to the MMA, scale and bias applied
+    // per group in fp32) where it was measured fastest on B200 (CUDA graphs of weight copies larger than L2, us a
+    // call, qmvq / qmvg / qmv): the fused QKV projection 6144 x 2560 at 1, 8 and 16 tokens (4.87 / 5.43 / 6.04,
+    // 5.05 / 5.74 / 5.98, 6.86 / 7.10 / 7.04), and up to 8 tokens for K <= 4096 (4096 x 4096: 6.01 / 6.64 / 6.89 at
+    // M=1; 9728 x 2560: 7.59 / 8.35 / 8.80 at M=1); qmv for the rest (2560 x 9728 at M=1: 10.63 against 12.67;
+    // 4096 x 4096 at M=16: 7.57 against 7.95)
+    const bool qmvq_auto = qmvq_shape_ok(M, K, bits) && (M <= 8 ? K <= 4096 : (K <= 2560 && N <= 8192));
+    if (fam == LQ_FAM_AUTO && qmvq_auto) {
+        const int p[4] = {0, 0, 0, 0};
+        rc = qmvq_run(x, w, s, b, nout, outs, a.seg_end, a.ldo, M, N, K, dtype, p, st);
         if (rc != LQ_E_SHAPE) return finish(rc);
     }
     if (!qmv_shape_ok(K, bits)) {
@@ -477,9 +488,10 @@ int lq_supported(int family, int M, int N, int K, int bits, int group_size, int 
     if (!is16(dtype) || (bits != 4 && bits != 8) || group_size != 64) return 0;
     if (M < 1 || N < 1 || K < 64 || K % 64) return 0;
     const bool qmv = qmv_shape_ok(K, bits), tcv = tcv_shape_ok(M, K, bits), tc = tc_shape_ok(M, N, K, bits);
-    const bool qmvg = qmvg_shape_ok(M, K, bits);
+    const bool qmvg = qmvg_shape_ok(M, K, bits), qmvq = qmvq_shape_ok(M, K, bits);
     switch (family) {
-        case LQ_FAM_AUTO: return (qmv || qmvg || tcv || (M > 64 && tc)) ? 1 : 0;
+        case LQ_FAM_AUTO: return (qmv || qmvg || qmvq || tcv || (M > 64 && tc)) ? 1 : 0;
+        case LQ_FAM_QMVQ: return qmvq ? 1 : 0;
         case LQ_FAM_QMV: return qmv ? 1 : 0;
         case LQ_FAM_QMVG: return qmvg ? 1 : 0;
         case LQ_FAM_TCV: return tcv ? 1 : 0;
@@ -520,6 +532,11 @@ int lq_list_configs(int M, int N, int K, int bits, int group_size, int dtype, lq
     if (lq_supported(LQ_FAM_QMVG, M, N, K, bits, group_size, dtype)) {
         add(LQ_FAM_QMVG, 0, 0, 0, 0);
         for (int fr = 1; fr <= 4; ++fr) add(LQ_FAM_QMVG, fr, 0, 0, 0);
+    }
+    if (lq_supported(LQ_FAM_QMVQ, M, N, K, bits, group_size, dtype)) {
+        add(LQ_FAM_QMVQ, 0, 0, 0, 0);
+        for (int sx = 1; sx <= 2; ++sx)
+            for (int fr = 0; fr <= 4; ++fr) add(LQ_FAM_QMVQ, fr, 0, 0, sx);
     }
     if (lq_supported(LQ_FAM_TCV, M, N, K, bits, group_size, dtype)) {
         add(LQ_FAM_TCV, 0, 0, 0, 0);

@@ -535,10 +535,12 @@ static int qmv_launch_t(const void* x, int x_rows, const QmvMats& mats, QmvArgs 
     if (fixed + S::STAGE_BYTES > budget) budget = di.smem_optin;
     int ns = int((budget - fixed) / S::STAGE_BYTES);
     if (ns < 1) return LQ_E_SHAPE;
+    // a requested depth may use the whole SM's shared memory (one CTA an SM, more bytes in flight)
+    if (ns_req > 0) ns = ns_req < int((di.smem_optin - fixed) / S::STAGE_BYTES) ? ns_req
+                                                                               : int((di.smem_optin - fixed) / S::STAGE_BYTES);
     if (ns > QMV_MAX_STAGES) ns = QMV_MAX_STAGES;
     const int max_tb = a.grouped ? 64 : (a.M + S::MTOK - 1) / S::MTOK;
     if (ns > per_cta * max_tb) ns = per_cta * max_tb;
-    if (ns_req > 0 && ns_req < ns) ns = ns_req;
     a.ns = ns;
     const size_t smem = fixed + size_t(ns) * S::STAGE_BYTES;
     if (smem > di.smem_optin) return LQ_E_SHAPE;

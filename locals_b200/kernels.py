@@ -13,6 +13,8 @@ every path is a hand-written sm_100a kernel of liblq.so:
   mma.sync fragments, cluster split-K), any M (weights streamed once per 64 rows);
 * ``("qmvg", FR, NS)`` -- dense 4-bit decode for M <= 16: each warp takes one 64-wide group of every stage for
   all of its CTA's 16-row fragments (x loaded once per group), fragments spread over every SM;
+* ``("qmvq", FR, NS)`` -- the same split with the codes fed raw to the MMA and each group's scale and bias folded in
+  fp32 (the reference's fragq formulation): the weights are never rounded to the activation dtype;
 * ``("tcv", NTOK, KS, WS[, PERSISTENT])`` -- the tensor-core family with weights dequantized into tensor
   memory as the MMA's A operand and tokens as its N side (16..256 columns); PERSISTENT = 1 runs one CTA
   per SM over all tiles (K % 256 == 0 at 4 bits);
@@ -91,7 +93,8 @@ def dequantize(wq: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, gro
 
 # ---- matmul ------------------------------------------------------------------------------------
 
-_FAMILY = {"auto": _lib.FAM_AUTO, "qmv": _lib.FAM_QMV, "tc": _lib.FAM_TC, "tcv": _lib.FAM_TCV, "qmvg": _lib.FAM_QMVG}
+_FAMILY = {"auto": _lib.FAM_AUTO, "qmv": _lib.FAM_QMV, "tc": _lib.FAM_TC, "tcv": _lib.FAM_TCV, "qmvg": _lib.FAM_QMVG,
+           "qmvq": _lib.FAM_QMVQ}
 
 
 def _cfg(choice: Optional[Sequence]):
@@ -205,7 +208,7 @@ def launch(choice: Sequence, M: int, K: int, N: int, dtype: torch.dtype, bits: i
 
 
 _FAMILY_NAME = {v: k for k, v in _FAMILY.items()}
-_NPARAM = {"qmv": 4, "tcv": 4, "tc": 1, "qmvg": 2}
+_NPARAM = {"qmv": 4, "tcv": 4, "tc": 1, "qmvg": 2, "qmvq": 4}
 
 
 def candidates(M: int, K: int, N: int, bits: int = 4, dtype: torch.dtype = torch.bfloat16) -> list:

@@ -94,12 +94,15 @@ def test_supported_and_candidates():
     assert L.lq_supported(4, 16, 6144, 2560, 4, 64, 1) == 1   # qmvg: 4-bit, M <= 16, K % 256 == 0
     assert L.lq_supported(4, 17, 6144, 2560, 4, 64, 1) == 0
     assert L.lq_supported(4, 16, 6144, 2560, 8, 64, 1) == 0
+    assert L.lq_supported(5, 16, 6144, 2560, 4, 64, 1) == 1   # qmvq: as qmvg
+    assert L.lq_supported(5, 17, 6144, 2560, 4, 64, 1) == 0
     assert L.lq_supported(7, 16, 6144, 2560, 4, 64, 1) == 0   # unknown family
     dec = kernels.candidates(16, 2560, 6144, 4)
     assert dec[0] == ("qmv", 0, 0, 0, 0) and ("tcv", 0, 0, 0, 0) in dec and ("tcv", 0, 0, 0, 1) in dec
     assert ("qmvg", 0, 0) in dec and ("qmvg", 4, 0) in dec
-    assert all(c[0] in ("qmv", "qmvg", "tcv") for c in dec)
-    assert all(c[0] != "qmvg" for c in kernels.candidates(32, 2560, 6144, 4))
+    assert ("qmvq", 0, 0, 0, 0) in dec and ("qmvq", 4, 0, 0, 2) in dec
+    assert all(c[0] in ("qmv", "qmvg", "qmvq", "tcv") for c in dec)
+    assert all(c[0] not in ("qmvg", "qmvq") for c in kernels.candidates(32, 2560, 6144, 4))
     pre = kernels.candidates(2048, 4096, 14336, 4)
     assert ("tc", 0) in pre and ("tc", 256) in pre and ("tcv", 256, 1, 0, 0) in pre
     assert ("dense",) in pre and ("dense", 224) in pre  # the reference's dequantize + dense GEMM path
