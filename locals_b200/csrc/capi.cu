@@ -49,7 +49,11 @@ int qmvg_run(const void* x, const uint32_t* w, const void* s, const void* b, int
              const int* seg_end, const int* ldo, int M, int N, int K, int dtype, const int* p, cudaStream_t st);
 bool qmvq_shape_ok(int M, int K, int bits);
 int qmvq_run(const void* x, const uint32_t* w, const void* s, const void* b, int nout, void* const* outs,
-             const int* seg_end, const int* ldo, int M, int N, int K, int dtype, const int* p, cudaStream_t st);
+             const int* seg_end, const int* ldo, int M, int N, int K, int bits, int dtype, const int* p,
+             cudaStream_t st);
+int qmvq_glu_run(const void* x, const uint32_t* w_gate, const void* s_gate, const void* b_gate, const uint32_t* w_up,
+                 const void* s_up, const void* b_up, void* h, int M, int I, int K, int bits, int dtype, const int* p,
+                 cudaStream_t st);
 bool qmvg_moe_ok(int mode, int k, int rows_e, int K, int sms);
 int qmvg_moe_run(int mode, const void* x, const int32_t* experts, const int32_t* pos, const float* wts,
                  const uint32_t* w0, const void* s0, const void* b0, const uint32_t* w1, const void* s1, const void* b1,
@@ -130,7 +134,7 @@ static int qmm_common(const void* x, const uint32_t* w, const void* s, const voi
     }
     if (fam == LQ_FAM_QMVQ) {
         if (!qmvq_shape_ok(M, K, bits)) return LQ_E_SHAPE;
-        return finish(qmvq_run(x, w, s, b, nout, outs, a.seg_end, a.ldo, M, N, K, dtype, cfg->p, st));
+        return finish(qmvq_run(x, w, s, b, nout, outs, a.seg_end, a.ldo, M, N, K, bits, dtype, cfg->p, st));
     }
     if (fam == LQ_FAM_QMVG) {
         if (!qmvg_shape_ok(M, K, bits)) return LQ_E_SHAPE;
@@ -155,10 +159,10 @@ static int qmm_common(const void* x, const uint32_t* w, const void* s, const voi
     // 5.05 / 5.74 / 5.98, 6.86 / 7.10 / 7.04), and up to 8 tokens for K <= 4096 (4096 x 4096: 6.01 / 6.64 / 6.89 at
     // M=1; 9728 x 2560: 7.59 / 8.35 / 8.80 at M=1); qmv for the rest (2560 x 9728 at M=1: 10.63 against 12.67;
     // 4096 x 4096 at M=16: 7.57 against 7.95)
-    const bool qmvq_auto = qmvq_shape_ok(M, K, bits) && (M <= 8 ? K <= 4096 : (K <= 2560 && N <= 8192));
+    const bool qmvq_auto = bits == 4 && qmvq_shape_ok(M, K, bits) && (M <= 8 ? K <= 4096 : (K <= 2560 && N <= 8192));
     if (fam == LQ_FAM_AUTO && qmvq_auto) {
         const int p[4] = {0, 0, 0, 0};
-        rc = qmvq_run(x, w, s, b, nout, outs, a.seg_end, a.ldo, M, N, K, dtype, p, st);
+        rc = qmvq_run(x, w, s, b, nout, outs, a.seg_end, a.ldo, M, N, K, bits, dtype, p, st);
         if (rc != LQ_E_SHAPE) return finish(rc);
     }
     if (!qmv_shape_ok(K, bits)) {
@@ -230,6 +234,11 @@ int lq_qmm_glu(const void* x, const uint32_t* w_gate, const void* s_gate, const 
     m.rows_total[0] = m.rows_total[1] = I;
     const int fam = cfg ? cfg->family : LQ_FAM_AUTO;
     void* outs[1] = {h};
+    if (fam == LQ_FAM_QMVQ) {
+        if (!qmvq_shape_ok(M, K, bits)) return LQ_E_SHAPE;
+        return finish(qmvq_glu_run(x, w_gate, s_gate, b_gate, w_up, s_up, b_up, h, M, I, K, bits, dtype, cfg->p,
+                                   reinterpret_cast<cudaStream_t>(stream)));
+    }
     if (fam == LQ_FAM_TCV) {
         if (cfg->p[3] == 1) {
             if (!tcvp_shape_ok(M, K, bits)) return LQ_E_SHAPE;
@@ -239,6 +248,14 @@ int lq_qmm_glu(const void* x, const uint32_t* w_gate, const void* s_gate, const 
         if (!tcv_shape_ok(M, K, bits)) return LQ_E_SHAPE;
         return finish(tcv_run(x, M, m, 2, I, K, 1, outs, a.seg_end, a.ldo, bits, dtype, cfg->p,
                               reinterpret_cast<cudaStream_t>(stream)));
+    }
+    // up to 16 tokens: gate and up in one folded kernel over every SM (B200, us a call on 9728 x 2560 pairs, qmvq
+    // against the previous choice: 8-bit 15.2 / 25.2 (qmv) at M=1, 21.1 / 24.0 (tcv) at M=16; 4-bit 11.5 / 14.6 at
+    // M=1, 14.5 / 22.1 at M=16)
+    if (fam == LQ_FAM_AUTO && qmvq_shape_ok(M, K, bits)) {
+        rc = qmvq_glu_run(x, w_gate, s_gate, b_gate, w_up, s_up, b_up, h, M, I, K, bits, dtype, nullptr,
+                          reinterpret_cast<cudaStream_t>(stream));
+        if (rc != LQ_E_SHAPE) return finish(rc);
     }
     if (fam == LQ_FAM_AUTO && prefer_tcv(M, 2.0 * I * K * bits / 8, K, bits)) {
         rc = tcv_run(x, M, m, 2, I, K, 1, outs, a.seg_end, a.ldo, bits, dtype, nullptr,

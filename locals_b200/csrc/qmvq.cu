@@ -1,23 +1,36 @@
-// Dense 4-bit decode with the codes fed raw to the MMA and scale and bias folded per group in fp32 ("qmvq" family):
-// y (M, N) = x (M, K) . dequant(W)^T for M <= 16 tokens. The B200 counterpart of the reference's fragq kernel
-// (locals/qmv_frag.py:368-540): there the codes enter the 8x8 MMA as 1 + q/16 in the mantissa and each group's scale
-// and bias are applied to the fp32 partial sum; here they enter mma.sync.m16n8k16 as 128 + q (bf16) or 1024 + q
-// (fp16) -- one lop3 with the magic exponent per code pair, no subtract, no fma -- and each 64-wide group ends with
-//     y += s * acc + (b - magic * s) * sum(x)
-// in fp32, where acc = sum((magic + q) x) over the group and sum(x) is the group's x sum, taken by one more MMA with
-// an all-ones A operand (so it lands in the accumulator layout the fold needs). The weights are never rounded to the
-// activation dtype: the result is the fp32 factoring s . sum(q x) + b . sum(x) of the reference's multi-row kernels
-// (locals/qmv_multi.py:57-75), which is what mx.quantized_matmul computes.
+// Decode with the codes fed raw to the MMA and scale and bias folded per group in fp32 ("qmvq" family):
+// y (M, N) = x (M, K) . dequant(W)^T for M <= 16 tokens, 4- or 8-bit codes, one matrix or a gate/up pair with the
+// SwiGLU epilogue. The B200 counterpart of the reference's fragq kernel (locals/qmv_frag.py:368-540): there the codes
+// enter the 8x8 MMA as 1 + q/16 in the mantissa and each group's scale and bias are applied to the fp32 partial sum;
+// here they enter mma.sync.m16n8k16 as magic + q -- magic = 128 in bf16, 1024 in fp16, one lop3 a code pair, no
+// subtract, no fma -- and each 64-wide group ends with
+//     y += s * acc + (b - magic * s) * sum(x)                       (4-bit: acc = sum((magic + q) x))
+//     y += s * (16 acc_hi + acc_lo) + (b - 17 magic s) * sum(x)      (8-bit: the high and low nibbles of each code
+//                                                                     enter two MMAs as magic + nibble)
+// in fp32, where sum(x) is the group's x sum, taken by one more MMA with an all-ones A operand (so it lands in the
+// accumulator layout the fold needs). The weights are never rounded to the activation dtype: the result is the fp32
+// factoring s . sum(q x) + b . sum(x) of the reference's multi-row kernels (locals/qmv_multi.py:57-75), which is what
+// mx.quantized_matmul computes.
 //
-// Work split as in the group-per-warp family (qmvg.cu): the N/16 row fragments dealt out evenly over every SM, one
-// ring stage = 512 K values of all of the CTA's rows (one TMA box), consumer warp w takes group w of every stage for
-// all of the CTA's fragments, the eight warps' partial sums added through shared memory at the end, x loaded by each
-// consumer lane straight into registers one stage ahead. Nothing the producer loads depends on the previous kernel,
-// so under programmatic dependent launch the whole ring fills before the dependency resolves. (A producer that also
-// widened each stage's scales into an fp32 (s, b - magic s) table was measured 1.8x slower on B200: one warp doing
-// that for every stage delays the ring and the dependent launch; the consumers widen their own two rows instead.)
+// Work split: the 16-row fragments of the matrix (or the (gate, up) fragment pairs) are dealt out evenly over every SM
+// (CTA c takes units [cU/C, (c+1)U/C)); one ring stage = 512 K values of all of the CTA's rows (one TMA box a matrix,
+// 128-byte swizzle); consumer warp w takes group w of every stage for all of the CTA's fragments, so its x fragments
+// are loaded and permuted once and reused for every fragment; the eight warps' partial sums are added through shared
+// memory at the end; x is loaded by each consumer lane straight into registers ahead of its use. Nothing the producer
+// loads depends on the previous kernel, so under programmatic dependent launch the ring fills while the previous
+// kernel runs. Two footprints: 4-bit single matrices keep to half an SM (two CTAs an SM: the next call's CTA loads
+// its weights beside the running one -- decode projections are a few MB); 8-bit matrices and gate/up pairs (tens of
+// MB a call) take the whole SM for a deeper ring and more registers.
+// Measured facts behind the choices (B200, CUDA graphs of weight copies larger than L2): a producer that also widened
+// each stage's scales into an fp32 table was 1.8x slower (one warp doing it delays the ring and the dependent launch);
+// x staged in shared memory by the lanes' own cp.async was slower than registers (7.0 and 7.3 against 4.8 us a layer
+// at one token); weights copied by the 256 consumer threads before the dependency were no faster than TMA; shared
+// reads as plain C++ loads were slower than these asm loads (5.10 against 4.90 us). A per-CTA %globaltimer timeline of
+// the fused QKV projection at one token: the dependency resolves 0.77 us after the previous call's last CTA ends (every
+// weight stage has landed by then), the first x stage 0.4 us later, five stages take 3.0 us of consumer issue (2 warps a
+// scheduler, latency-bound: 29% issue active under ncu), the reduction and stores 0.6 us.
 // Reference: the multi-row GEMV it replaces, locals/qmv_frag.py:368-540 (fragq) behind kernels._launcher
-// (locals/kernels.py:516-576).
+// (locals/kernels.py:516-576), and the fused MLP's gate/up projection (locals/fuse.py:160-164, locals/moe.py:284-289).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -33,38 +46,49 @@ namespace lq {
 
 constexpr int QQ_CW = 8;  // consumer warps: group w of every 8-group stage
 constexpr int QQ_THREADS = 32 * (QQ_CW + 1);
-constexpr int QQ_MAX_STAGES = 6;
-constexpr int QQ_MAX_FR = 4;
+constexpr int QQ_MAX_STAGES = 8;
 
-template <int MT, int FR>
+// Two CTAs an SM (4-bit single matrices) or one (8-bit, gate/up pairs). (A second set of eight consumer warps taking
+// alternate fragments, which one CTA an SM has the registers for, measured slower on B200: 17.9 against 15.2 us for
+// the 8-bit gate/up pair at one token.)
+template <int BITS, int NMAT>
+struct QqFoot {
+    static constexpr bool kHalf = BITS == 4 && NMAT == 1;
+    static constexpr int kMinBlocks = kHalf ? 2 : 1;
+    static constexpr int kMaxFr = kHalf ? 4 : 6;
+};
+
+template <int BITS, int MT, int FR, int NMAT>
 struct QqShape {
     static constexpr int MTOK = 8 * MT;                  // token slots
-    static constexpr int W_FRAG = 16 * 256;              // one 16-row fragment: 256 bytes (512 codes) a row
-    static constexpr int W_BYTES = FR * W_FRAG;
-    static constexpr int SB_BYTES = FR * 16 * 16;        // scales (or biases): rows x 8 groups x 2 bytes
-    static constexpr int STAGE_BYTES = (W_BYTES + 2 * SB_BYTES + 1023) / 1024 * 1024;
-    // the warps' partial sums [warp][token][FR * 16 rows + 4]: the 4-float pad puts the four token columns a lane
-    // quad writes at once 8 banks apart, so every partial-sum store of a warp is free of bank conflicts
-    static constexpr int RRP = FR * 16 + 4;
+    static constexpr int RB = BITS * 64;                 // bytes of a row a stage (512 K values)
+    static constexpr int SEGS = RB / 128;                // 128-byte swizzle segments a row
+    static constexpr int W_FRAG = 16 * RB;               // one 16-row fragment
+    static constexpr int W_MAT = FR * W_FRAG;            // one matrix's box
+    static constexpr int W_BYTES = NMAT * W_MAT;
+    static constexpr int SB_MAT = FR * 16 * 16;          // one matrix's scales (or biases): rows x 8 groups x 2 bytes
+    static constexpr int SB_OFF = W_BYTES;               // matrix m's scales at SB_OFF + 2 m SB_MAT, biases + SB_MAT
+    static constexpr int STAGE_BYTES = (W_BYTES + NMAT * 2 * SB_MAT + 1023) / 1024 * 1024;
+    // the warps' partial sums [warp][token][NMAT * FR * 16 rows + 4]: the 4-float pad puts the four token columns a
+    // lane quad writes at once 8 banks apart, so every partial-sum store of a warp is free of bank conflicts
+    static constexpr int RRP = NMAT * FR * 16 + 4;
     static constexpr int RED_BYTES = QQ_CW * MTOK * RRP * 4;
-    // x loaded DX stages ahead of its use: two for up to 8 tokens, one for 16 (the register budget of two CTAs an SM)
+    // x loaded DX stages ahead of its use: two for up to 8 tokens, one for 16 (the register budget)
     static constexpr int DX = MT == 1 ? 2 : 1;
     static_assert(W_FRAG % 1024 == 0, "1 KB alignment of swizzled tiles");
 };
 
 struct QqArgs {
-    int M, N, K;
-    int kg;      // groups a row (K / 64)
-    int nchunk;  // stages of 512 K values
-    int nfrag;   // 16-row fragments (ceil(N / 16))
-    int ns;      // ring depth
-    int sb_vec;  // cp.async width for scale / bias rows
-    int cpw;     // 1: the consumer threads copy the weights (cp.async, before the grid dependency), 0: TMA
-    const uint32_t* w;
+    int M, N, K;   // N: rows of each matrix
+    int kg;        // groups a row (K / 64)
+    int nchunk;    // stages of 512 K values
+    int units;     // 16-row fragments of each matrix (ceil(N / 16))
+    int ns;        // ring depth
+    int sb_vec;    // cp.async width for scale / bias rows
     const void* x;
-    const void* s;
-    const void* b;
-    void* out[3];  // output column segments (fused q / k / v), or out[0] only
+    const void* s[2];
+    const void* b[2];
+    void* out[3];  // output column segments (fused q / k / v), or out[0] only (h for gate/up pairs)
     int seg_end[3];
     int ldo[3];
     int nseg_out;
@@ -90,6 +114,12 @@ struct QqMagic<__half> {
 __device__ __forceinline__ uint2 qq_lds64(uint32_t addr) {
     uint2 v;
     asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ uint4 qq_lds128(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
     return v;
 }
 
@@ -126,16 +156,34 @@ __device__ __forceinline__ void qq_store(const QqArgs& a, int row, int n, float 
         reinterpret_cast<__half*>(base)[off] = __float2half_rn(v);
 }
 
-// SXA: the group's x sums by fp32 adds and quad shuffles (true) or by an MMA with an all-ones A operand (false)
-template <typename T, int MT, int FR, bool SXA>
-__global__ void __launch_bounds__(QQ_THREADS, 2)
-    qmvq_kernel(const __grid_constant__ CUtensorMap tm_w_full, const __grid_constant__ CUtensorMap tm_w_less,
-                const QqArgs a) {
-    using S = QqShape<MT, FR>;
+template <typename T>
+__device__ __forceinline__ float qq_round(float v) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value)
+        return __bfloat162float(__float2bfloat16_rn(v));
+    else
+        return __half2float(__float2half_rn(v));
+}
+
+// silu(g) * u with the activation-dtype rounding points of locals/moe.py:284-289 (the store rounds the product)
+template <typename T>
+__device__ __forceinline__ float qq_swiglu(float g, float u) {
+    const float gt = qq_round<T>(g), ut = qq_round<T>(u);
+    const float sig = qq_round<T>(1.0f / (1.0f + expf(-gt)));
+    return qq_round<T>(gt * sig) * ut;
+}
+
+// SXA: the group's x sums by fp32 adds and quad shuffles (true) or by an MMA with an all-ones A operand (false).
+// Matrix m's weight boxes: tm0 / tm2 (CTAs holding FR units) and tm1 / tm3 (FR - 1 units).
+template <typename T, int BITS, int MT, int FR, int NMAT, bool SXA>
+__global__ void __launch_bounds__(QQ_THREADS, QqFoot<BITS, NMAT>::kMinBlocks)
+    qmvq_kernel(const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1,
+                const __grid_constant__ CUtensorMap tm2, const __grid_constant__ CUtensorMap tm3, const QqArgs a) {
+    using S = QqShape<BITS, MT, FR, NMAT>;
     using TR = F16Traits<T>;
     using MG = QqMagic<T>;
     constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
     constexpr int RING_MIN = S::RED_BYTES;  // the ring is reused for the partial sums
+    constexpr float kFold = BITS == 4 ? MG::kVal : 17.0f * MG::kVal;
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -145,22 +193,20 @@ __global__ void __launch_bounds__(QQ_THREADS, 2)
     uint64_t* empty = full + QQ_MAX_STAGES;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // fragments [f0, f0 + nf): a CTA holds FR or FR - 1 of them (host-chosen grid)
-    const int f0 = int((long long)blockIdx.x * a.nfrag / gridDim.x);
-    const int nf = int((long long)(blockIdx.x + 1) * a.nfrag / gridDim.x) - f0;
-    if (nf < 1 || nf > FR || nf < FR - 1) {  // the weight boxes hold 16 FR or 16 (FR - 1) rows: nothing else fits
+    // units [u0, u0 + nu): a CTA holds FR or FR - 1 of them (host-chosen grid)
+    const int u0 = int((long long)blockIdx.x * a.units / gridDim.x);
+    const int nu = int((long long)(blockIdx.x + 1) * a.units / gridDim.x) - u0;
+    if (nu < 1 || nu > FR || nu < FR - 1) {  // the weight boxes hold 16 FR or 16 (FR - 1) rows: nothing else fits
         if (threadIdx.x == 0) record_status(LQ_DEV_BOUNDS);
         return;
     }
-    const int row0 = 16 * f0;
+    const int row0 = 16 * u0;
     const int total = a.nchunk;
     const int mv = a.M < S::MTOK ? a.M : S::MTOK;  // real token rows
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ns; ++s) {
-            // TMA: lane 0's expect_tx arrive + the producer lanes' cp.async arrivals (scales); consumer-copied
-            // weights: the producer lanes' and every consumer thread's cp.async arrivals
-            mbar_init(&full[s], a.cpw ? 32 + 32 * QQ_CW : 1 + 32);
+            mbar_init(&full[s], 1 + 32);  // lane 0's expect_tx arrive + 32 cp.async arrivals
             mbar_init(&empty[s], QQ_CW);
         }
         fence_barrier_init();
@@ -171,30 +217,35 @@ __global__ void __launch_bounds__(QQ_THREADS, 2)
     if (warp == QQ_CW) {
         // ------------------------------ producer warp ------------------------------
         const uint64_t pol_w = policy_evict_first();
-        const CUtensorMap* tm_w = nf == FR ? &tm_w_full : &tm_w_less;
+        const CUtensorMap* tmw[2] = {nu == FR ? &tm0 : &tm1, nu == FR ? &tm2 : &tm3};
         if (lane == 0) {
-            prefetch_tmap(&tm_w_full);
-            prefetch_tmap(&tm_w_less);
+            prefetch_tmap(tmw[0]);
+            if (NMAT == 2) prefetch_tmap(tmw[1]);
         }
         const uint32_t smem_base = smem_u32(smem);
         const int vb = a.sb_vec;
         const int units = 16 / vb;
         auto load = [&](int c, int s) {
             uint8_t* st = smem + s * S::STAGE_BYTES;
-            if (lane == 0 && !a.cpw) {
-                mbar_arrive_expect_tx(&full[s], nf * S::W_FRAG);
-                tma_load_3d(st, tm_w, &full[s], 0, row0, 2 * c, pol_w);
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&full[s], NMAT * nu * S::W_FRAG);
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m)
+                    tma_load_3d(st + m * S::W_MAT, tmw[m], &full[s], 0, row0, S::SEGS * c, pol_w);
             }
-            const uint32_t sdst = smem_base + s * S::STAGE_BYTES + S::W_BYTES;
-            for (int r = lane; r < nf * 16; r += 32) {
-                const int grow = row0 + r;
-                for (int u = 0; u < units; ++u) {
-                    const int gcol = 8 * c + u * (vb >> 1);
-                    const bool valid = grow < a.N && gcol < a.kg;
-                    const size_t off = valid ? (size_t(grow) * a.kg + gcol) * 2 : 0;
-                    const uint32_t d = sdst + r * 16 + u * vb;
-                    cp_async(d, reinterpret_cast<const uint8_t*>(a.s) + off, vb, valid);
-                    cp_async(d + S::SB_BYTES, reinterpret_cast<const uint8_t*>(a.b) + off, vb, valid);
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) {
+                const uint32_t sdst = smem_base + s * S::STAGE_BYTES + S::SB_OFF + m * 2 * S::SB_MAT;
+                for (int r = lane; r < nu * 16; r += 32) {
+                    const int grow = row0 + r;
+                    for (int u = 0; u < units; ++u) {
+                        const int gcol = 8 * c + u * (vb >> 1);
+                        const bool valid = grow < a.N && gcol < a.kg;
+                        const size_t off = valid ? (size_t(grow) * a.kg + gcol) * 2 : 0;
+                        const uint32_t d = sdst + r * 16 + u * vb;
+                        cp_async(d, reinterpret_cast<const uint8_t*>(a.s[m]) + off, vb, valid);
+                        cp_async(d + S::SB_MAT, reinterpret_cast<const uint8_t*>(a.b[m]) + off, vb, valid);
+                    }
                 }
             }
             cp_async_arrive(&full[s]);
@@ -214,46 +265,34 @@ __global__ void __launch_bounds__(QQ_THREADS, 2)
     }
 
     // ------------------------------ consumer warps ------------------------------
-    const uint32_t smem_base = smem_u32(smem);
-    if (a.cpw) {
-        // Every stage's packed words by the consumer threads' own 16-byte cp.async, issued before the grid dependency
-        // (they do not depend on the previous kernel), into the layout the TMA box would give: chunk c of row r at
-        // segment c / 8, 128 r + 16 ((c % 8) ^ (r % 8)). Zero-filled past N and past K. Only used when the ring holds
-        // every stage (the host checks).
-        const uint8_t* wb = reinterpret_cast<const uint8_t*>(a.w);
-        const size_t row_bytes = size_t(a.K) / 2;
-        for (int i = 0; i < total; ++i) {
-            const uint32_t st = smem_base + i * S::STAGE_BYTES;
-            for (int idx = threadIdx.x; idx < nf * 16 * 16; idx += 32 * QQ_CW) {
-                const int r = idx >> 4, c = idx & 15;
-                const bool valid = row0 + r < a.N && i * 512 + c * 32 < a.K;
-                const uint8_t* src = valid ? wb + size_t(row0 + r) * row_bytes + i * 256 + c * 16 : wb;
-                cp_async(st + (c >> 3) * (nf * 2048) + r * 128 + (((c & 7) ^ (r & 7)) << 4), src, 16, valid);
-            }
-            cp_async_arrive(&full[i]);
-        }
-    }
     grid_dep_wait();  // x may be the previous kernel's output (and before any output store of this kernel)
     const int g = lane >> 2, t = lane & 3;
-    float acc[FR][MT][4];
+    const uint32_t smem_base = smem_u32(smem);
+    float acc[NMAT][FR][MT][4];
 #pragma unroll
-    for (int f = 0; f < FR; ++f)
+    for (int m = 0; m < NMAT; ++m)
 #pragma unroll
-        for (int q = 0; q < MT; ++q)
+        for (int f = 0; f < FR; ++f)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) acc[f][q][e] = 0.0f;
+            for (int q = 0; q < MT; ++q)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[m][f][q][e] = 0.0f;
 
-    // this lane's 8 bytes of a row inside group w of a stage (128-byte swizzle: 16-byte chunk c of row r sits at
-    // c ^ (r & 7)); the stage's box is [segment][16 nf rows][128 bytes], fragment f's rows at 2048 f of each segment
-    const uint32_t w_off =
-        (warp >> 2) * (nf * 2048) + g * 128 + (((2 * (warp & 3) + (t >> 1)) ^ g) << 4) + 8 * (t & 1);
+    // The row of a fragment this lane reads (and r + 8): 4-bit lanes read 8 bytes of row g; 8-bit lanes read 16 bytes
+    // of row (g >> 1) | ((g & 1) << 2), so the two rows a quarter-warp reads at once sit in different halves of the
+    // 128-byte swizzle atom (no bank conflicts); the MMA's row g then holds that weight row.
+    const int r_lo = BITS == 4 ? g : ((g >> 1) | ((g & 1) << 2));
+    // this lane's bytes of a row inside group w of a stage (128-byte swizzle: 16-byte chunk c of row r sits at
+    // c ^ (r & 7)); a matrix's box is [segment][16 nu rows][128 bytes], fragment f's rows at 2048 f of each segment
+    const uint32_t w_off = BITS == 4
+                               ? (warp >> 2) * (nu * 2048) + r_lo * 128 + (((2 * (warp & 3) + (t >> 1)) ^ r_lo) << 4) +
+                                     8 * (t & 1)
+                               : (warp >> 1) * (nu * 2048) + r_lo * 128 + (((4 * (warp & 1) + t) ^ r_lo) << 4);
     // x of stage i's group for this lane: values 16t .. 16t + 15 of tokens g + 8 mt (zero past M and past K), loaded
-    // straight into registers ahead of its use. (Staging x in shared memory by the lanes' own cp.async
-    // instead -- every stage at once, or one ahead -- measured slower on B200: 7.0 and 7.3 us against 4.8 us a layer
-    // on the one-token QKV projection.)
+    // straight into registers ahead of its use. Token columns past M keep whatever their registers held: an MMA's
+    // output column n depends on its input column n only (the x sums too), and those columns are never stored. Stages
+    // past K are skipped whole.
     const uint8_t* xg = reinterpret_cast<const uint8_t*>(a.x);
-    // Token columns past M keep whatever their registers held: an MMA's output column n depends on its input column n
-    // only (the x sums too), and those columns are never stored. Stages past K are skipped whole.
     auto fetch_x = [&](int i, uint4 (&u)[MT][2]) {
         const int gi = 8 * i + warp;
 #pragma unroll
@@ -284,27 +323,28 @@ __global__ void __launch_bounds__(QQ_THREADS, 2)
         if (ok) ok = mbar_wait(&full[s], (i / ns) & 1);
         if (ok && 8 * i + warp < a.kg) {
             const uint32_t st = smem_base + s * S::STAGE_BYTES;
-            // x fragments of group w permuted to the code order, and the group's x sums in the accumulator layout
-            // (sx[mt][e] = sum(x) of token column 2t + (e & 1); rows are alike, so entries 2 and 3 go unused)
+            // x fragments of group w permuted to the code order of a k16 step, and the group's x sums in the
+            // accumulator layout (sx[mt][e] = sum(x) of token column 2t + (e & 1); rows are alike, entries 2 and 3 go
+            // unused). 4-bit: step s takes codes (p, p + 4) of word s / 2 (p = 2 (s & 1), + 1), i.e. x words
+            // (s / 2 * 4 + s % 2, + 2); 8-bit: step s takes word s's bytes (0, 2) and (1, 3), i.e. x words (2s, 2s + 1).
             uint32_t xb[MT][4][2];
             float sx[MT][4];
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) {
-                const uint4 u0 = xc[mt][0], u1 = xc[mt][1];
-                xb[mt][0][0] = prmt(u0.x, u0.z, 0x5410);
-                xb[mt][0][1] = prmt(u0.x, u0.z, 0x7632);
-                xb[mt][1][0] = prmt(u0.y, u0.w, 0x5410);
-                xb[mt][1][1] = prmt(u0.y, u0.w, 0x7632);
-                xb[mt][2][0] = prmt(u1.x, u1.z, 0x5410);
-                xb[mt][2][1] = prmt(u1.x, u1.z, 0x7632);
-                xb[mt][3][0] = prmt(u1.y, u1.w, 0x5410);
-                xb[mt][3][1] = prmt(u1.y, u1.w, 0x7632);
+                const uint32_t xw[8] = {xc[mt][0].x, xc[mt][0].y, xc[mt][0].z, xc[mt][0].w,
+                                        xc[mt][1].x, xc[mt][1].y, xc[mt][1].z, xc[mt][1].w};
+#pragma unroll
+                for (int step = 0; step < 4; ++step) {
+                    const int wa = BITS == 4 ? (step >> 1) * 4 + (step & 1) : 2 * step;
+                    const int wb = BITS == 4 ? wa + 2 : wa + 1;
+                    xb[mt][step][0] = prmt(xw[wa], xw[wb], 0x5410);
+                    xb[mt][step][1] = prmt(xw[wa], xw[wb], 0x7632);
+                }
                 if constexpr (SXA) {
                     // this lane's 16 values of token g + 8 mt, then the quad's 64, then moved to columns 2t, 2t + 1
-                    const uint32_t wv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
                     float sum = 0.0f;
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) sum += TR::to_f32(wv[j] & 0xFFFFu) + TR::to_f32(wv[j] >> 16);
+                    for (int j = 0; j < 8; ++j) sum += TR::to_f32(xw[j] & 0xFFFFu) + TR::to_f32(xw[j] >> 16);
                     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
                     sum += __shfl_xor_sync(0xffffffffu, sum, 2);
                     const float s0 = __shfl_sync(0xffffffffu, sum, 8 * t), s1 = __shfl_sync(0xffffffffu, sum, 8 * t + 4);
@@ -321,43 +361,78 @@ __global__ void __launch_bounds__(QQ_THREADS, 2)
                                   xb[mt][step][1]);
                 }
             }
-            const uint32_t sb = st + S::W_BYTES + 2 * warp;  // group w's scale of row r at sb + 16 r
-            // All FR fragments run without a branch (one straight block). A CTA holding nf = FR - 1 fragments
-            // computes one extra fragment from stale bytes of its own stage: every address stays inside the stage's
-            // weight box and tables, and its partial sums land in reduction rows the final sum never reads.
+            // All fragments run without a branch (one straight block). A CTA holding nu = FR - 1 units computes one
+            // extra fragment a matrix from stale bytes of its own stage: every address stays inside the stage's
+            // weight boxes and tables, and its partial sums land in reduction rows the final sum never reads.
 #pragma unroll
-            for (int f = 0; f < FR; ++f) {
-                const uint32_t fb = st + f * 2048 + w_off;
-                const uint2 wa = qq_lds64(fb), wb = qq_lds64(fb + 8 * 128);
-                // rows g and g + 8: (s, b - magic s) in fp32
-                const int ra = 16 * f + g, rb = ra + 8;
-                const float sa = TR::to_f32(lds_u16(sb + ra * 16)), sbb = TR::to_f32(lds_u16(sb + rb * 16));
-                const float2 pa = make_float2(sa, fmaf(-MG::kVal, sa, TR::to_f32(lds_u16(sb + S::SB_BYTES + ra * 16))));
-                const float2 pb = make_float2(sbb, fmaf(-MG::kVal, sbb, TR::to_f32(lds_u16(sb + S::SB_BYTES + rb * 16))));
-                float part[MT][4];
+            for (int m = 0; m < NMAT; ++m) {
+                const uint32_t sb = st + S::SB_OFF + m * 2 * S::SB_MAT + 2 * warp;  // group w's scale of row r: sb + 16 r
 #pragma unroll
-                for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) part[mt][e] = 0.0f;
-#pragma unroll
-                for (int step = 0; step < 4; ++step) {
-                    const uint32_t va = step < 2 ? wa.x : wa.y, vbw = step < 2 ? wb.x : wb.y;
-                    const int sh = 8 * (step & 1);  // codes (p, p + 4) and (p + 1, p + 5), p = 2 (step & 1)
-                    const uint32_t a0 = lop3_and_or(va >> sh, 0x000F000Fu, MG::kCode2);
-                    const uint32_t a2 = lop3_and_or(va >> (sh + 4), 0x000F000Fu, MG::kCode2);
-                    const uint32_t a1 = lop3_and_or(vbw >> sh, 0x000F000Fu, MG::kCode2);
-                    const uint32_t a3 = lop3_and_or(vbw >> (sh + 4), 0x000F000Fu, MG::kCode2);
+                for (int f = 0; f < FR; ++f) {
+                    const uint32_t fb = st + m * S::W_MAT + f * 2048 + w_off;
+                    // rows r_lo and r_lo + 8: s and b - fold * s in fp32
+                    const int ra = 16 * f + r_lo, rb = ra + 8;
+                    const float sa = TR::to_f32(lds_u16(sb + ra * 16)), sbb = TR::to_f32(lds_u16(sb + rb * 16));
+                    const float ca = fmaf(-kFold, sa, TR::to_f32(lds_u16(sb + S::SB_MAT + ra * 16)));
+                    const float cb = fmaf(-kFold, sbb, TR::to_f32(lds_u16(sb + S::SB_MAT + rb * 16)));
+                    float part[MT][4];
 #pragma unroll
                     for (int mt = 0; mt < MT; ++mt)
-                        qq_mma<T>(part[mt], a0, a1, a2, a3, xb[mt][step][0], xb[mt][step][1]);
-                }
-                // y += s * acc + (b - magic s) * sum(x), rows g (pa) and g + 8 (pb)
 #pragma unroll
-                for (int mt = 0; mt < MT; ++mt) {
-                    acc[f][mt][0] = fmaf(pa.x, part[mt][0], fmaf(pa.y, sx[mt][0], acc[f][mt][0]));
-                    acc[f][mt][1] = fmaf(pa.x, part[mt][1], fmaf(pa.y, sx[mt][1], acc[f][mt][1]));
-                    acc[f][mt][2] = fmaf(pb.x, part[mt][2], fmaf(pb.y, sx[mt][0], acc[f][mt][2]));
-                    acc[f][mt][3] = fmaf(pb.x, part[mt][3], fmaf(pb.y, sx[mt][1], acc[f][mt][3]));
+                        for (int e = 0; e < 4; ++e) part[mt][e] = 0.0f;
+                    if constexpr (BITS == 4) {
+                        const uint2 wa = qq_lds64(fb), wb = qq_lds64(fb + 8 * 128);
+#pragma unroll
+                        for (int step = 0; step < 4; ++step) {
+                            const uint32_t va = step < 2 ? wa.x : wa.y, vbw = step < 2 ? wb.x : wb.y;
+                            const int sh = 8 * (step & 1);  // codes (p, p + 4) and (p + 1, p + 5), p = 2 (step & 1)
+                            const uint32_t a0 = lop3_and_or(va >> sh, 0x000F000Fu, MG::kCode2);
+                            const uint32_t a2 = lop3_and_or(va >> (sh + 4), 0x000F000Fu, MG::kCode2);
+                            const uint32_t a1 = lop3_and_or(vbw >> sh, 0x000F000Fu, MG::kCode2);
+                            const uint32_t a3 = lop3_and_or(vbw >> (sh + 4), 0x000F000Fu, MG::kCode2);
+#pragma unroll
+                            for (int mt = 0; mt < MT; ++mt)
+                                qq_mma<T>(part[mt], a0, a1, a2, a3, xb[mt][step][0], xb[mt][step][1]);
+                        }
+                    } else {
+                        // 16 codes a row: word s holds the codes of step s, bytes (0, 2) and (1, 3) the MMA's k pairs
+                        const uint4 wa = qq_lds128(fb), wb = qq_lds128(fb + 8 * 128);
+                        const uint32_t va4[4] = {wa.x, wa.y, wa.z, wa.w}, vb4[4] = {wb.x, wb.y, wb.z, wb.w};
+                        float hi[MT][4];
+#pragma unroll
+                        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) hi[mt][e] = 0.0f;
+#pragma unroll
+                        for (int step = 0; step < 4; ++step) {
+                            const uint32_t va = va4[step], vbw = vb4[step];
+                            const uint32_t l0 = lop3_and_or(va, 0x000F000Fu, MG::kCode2);
+                            const uint32_t l2 = lop3_and_or(va >> 8, 0x000F000Fu, MG::kCode2);
+                            const uint32_t l1 = lop3_and_or(vbw, 0x000F000Fu, MG::kCode2);
+                            const uint32_t l3 = lop3_and_or(vbw >> 8, 0x000F000Fu, MG::kCode2);
+                            const uint32_t h0 = lop3_and_or(va >> 4, 0x000F000Fu, MG::kCode2);
+                            const uint32_t h2 = lop3_and_or(va >> 12, 0x000F000Fu, MG::kCode2);
+                            const uint32_t h1 = lop3_and_or(vbw >> 4, 0x000F000Fu, MG::kCode2);
+                            const uint32_t h3 = lop3_and_or(vbw >> 12, 0x000F000Fu, MG::kCode2);
+#pragma unroll
+                            for (int mt = 0; mt < MT; ++mt) {
+                                qq_mma<T>(part[mt], l0, l1, l2, l3, xb[mt][step][0], xb[mt][step][1]);
+                                qq_mma<T>(hi[mt], h0, h1, h2, h3, xb[mt][step][0], xb[mt][step][1]);
+                            }
+                        }
+#pragma unroll
+                        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) part[mt][e] = fmaf(16.0f, hi[mt][e], part[mt][e]);
+                    }
+                    // y += s * acc + (b - fold s) * sum(x), rows r_lo (a) and r_lo + 8 (b)
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) {
+                        acc[m][f][mt][0] = fmaf(sa, part[mt][0], fmaf(ca, sx[mt][0], acc[m][f][mt][0]));
+                        acc[m][f][mt][1] = fmaf(sa, part[mt][1], fmaf(ca, sx[mt][1], acc[m][f][mt][1]));
+                        acc[m][f][mt][2] = fmaf(sbb, part[mt][2], fmaf(cb, sx[mt][0], acc[m][f][mt][2]));
+                        acc[m][f][mt][3] = fmaf(sbb, part[mt][3], fmaf(cb, sx[mt][1], acc[m][f][mt][3]));
+                    }
                 }
             }
         }
@@ -376,26 +451,35 @@ __global__ void __launch_bounds__(QQ_THREADS, 2)
 
     // ---- the eight warps' partial sums, added through shared memory (the ring is free: every stage was consumed) ----
     named_barrier(1, 32 * QQ_CW);
-    float* red = reinterpret_cast<float*>(smem);  // [warp][token][FR * 16 rows + pad]
+    float* red = reinterpret_cast<float*>(smem);  // [warp][token][NMAT * FR * 16 rows + pad]
 #pragma unroll
-    for (int f = 0; f < FR; ++f)
+    for (int m = 0; m < NMAT; ++m)
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
+        for (int f = 0; f < FR; ++f)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int row = 16 * f + g + 8 * (e >> 1), tok = 8 * mt + 2 * t + (e & 1);
-                red[(warp * S::MTOK + tok) * S::RRP + row] = acc[f][mt][e];
-            }
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int row = (m * FR + f) * 16 + r_lo + 8 * (e >> 1), tok = 8 * mt + 2 * t + (e & 1);
+                    red[(warp * S::MTOK + tok) * S::RRP + row] = acc[m][f][mt][e];
+                }
     named_barrier(1, 32 * QQ_CW);
-    const int R = nf * 16;
+    auto sum_warps = [&](int tok, int row) {
+        float p[QQ_CW];  // the eight partial sums loaded together, then added as a tree
+#pragma unroll
+        for (int w = 0; w < QQ_CW; ++w) p[w] = red[(w * S::MTOK + tok) * S::RRP + row];
+        return ((p[0] + p[1]) + (p[2] + p[3])) + ((p[4] + p[5]) + (p[6] + p[7]));
+    };
+    const int R = nu * 16;
     for (int idx = threadIdx.x; idx < R * mv; idx += 32 * QQ_CW) {
         const int tok = idx / R, row = idx - tok * R;
         const int n = row0 + row;
         if (n >= a.N) continue;
-        float p[QQ_CW];  // the eight partial sums loaded together, then added as a tree
-#pragma unroll
-        for (int w = 0; w < QQ_CW; ++w) p[w] = red[(w * S::MTOK + tok) * S::RRP + row];
-        const float v = ((p[0] + p[1]) + (p[2] + p[3])) + ((p[4] + p[5]) + (p[6] + p[7]));
+        float v;
+        if constexpr (NMAT == 2)
+            v = qq_swiglu<T>(sum_warps(tok, row), sum_warps(tok, FR * 16 + row));
+        else
+            v = sum_warps(tok, row);
         if (ok) qq_store(a, tok, n, v, kBF16);
     }
 }
@@ -404,15 +488,16 @@ __global__ void __launch_bounds__(QQ_THREADS, 2)
 // host side
 // ------------------------------------------------------------------------------------------------
 
-template <typename T, int MT, int FR, bool SXA>
-static int qmvq_launch_t(const void* x, const uint32_t* w, QqArgs a, int ns_req, int nctas, cudaStream_t st) {
-    using S = QqShape<MT, FR>;
+template <typename T, int BITS, int MT, int FR, int NMAT, bool SXA>
+static int qmvq_launch_t(const uint32_t* const* w, QqArgs a, int ns_req, int nctas, cudaStream_t st) {
+    using S = QqShape<BITS, MT, FR, NMAT>;
     const DeviceInfo& di = device_info();
     const int K = a.K;
-    // stages: within half an SM's shared memory, so the next launch's CTA can start beside a running one
+    // stages: half an SM's shared memory for the two-CTA footprint (so the next call's CTA can start beside a running
+    // one), else the whole SM
     const size_t fixed = 2 * QQ_MAX_STAGES * 8 + 1024;
-    const size_t budget = di.smem_per_sm / 2 - 1024;
-    int ns = int((budget - fixed) / S::STAGE_BYTES);
+    const size_t budget = QqFoot<BITS, NMAT>::kHalf ? di.smem_per_sm / 2 - 1024 : di.smem_optin;
+    int ns = budget > fixed ? int((budget - fixed) / S::STAGE_BYTES) : 0;
     if (ns > QQ_MAX_STAGES) ns = QQ_MAX_STAGES;
     if (ns > a.nchunk) ns = a.nchunk;
     if (ns_req > 0 && ns_req < ns) ns = ns_req;
@@ -422,27 +507,27 @@ static int qmvq_launch_t(const void* x, const uint32_t* w, QqArgs a, int ns_req,
     if (ring < size_t(S::RED_BYTES)) ring = S::RED_BYTES;
     const size_t smem = ring + fixed;
     if (smem > di.smem_optin) return LQ_E_SHAPE;
-    if (a.cpw && ns < a.nchunk) a.cpw = 0;  // consumer-copied weights: only when the ring holds every stage
 
-    // weight boxes of 16 FR rows (CTAs holding FR fragments) and 16 (FR - 1) rows (the others); two 128-byte
-    // segments a stage
-    CUtensorMap tw[2];
-    for (int m = 0; m < 2; ++m) {
-        const int rows = 16 * (m == 0 || FR == 1 ? FR : FR - 1);
-        const uint64_t dims[3] = {32, uint64_t(a.N), uint64_t(K) / 256};
-        const uint64_t str[2] = {uint64_t(K) / 2, 128};
-        const uint32_t box[3] = {32, uint32_t(rows), 2};
-        const int rc = make_tmap(&tw[m], CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, w, dims, str, box,
-                                 CU_TENSOR_MAP_SWIZZLE_128B);
-        if (rc) return rc;
-    }
-    a.x = x;
-    a.w = w;
+    // weight boxes of 16 FR rows (CTAs holding FR units) and 16 (FR - 1) rows (the others) for each matrix; S::SEGS
+    // 128-byte segments a stage
+    CUtensorMap tw[4];
+    for (int m = 0; m < 2; ++m)
+        for (int h = 0; h < 2; ++h) {
+            const int rows = 16 * (h == 0 || FR == 1 ? FR : FR - 1);
+            const uint64_t dims[3] = {32, uint64_t(a.N), uint64_t(K) * BITS / 1024};
+            const uint64_t str[2] = {uint64_t(K) * BITS / 8, 128};
+            const uint32_t box[3] = {32, uint32_t(rows), uint32_t(S::SEGS)};
+            const int rc = make_tmap(&tw[2 * m + h], CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, w[m < NMAT ? m : 0], dims, str,
+                                     box, CU_TENSOR_MAP_SWIZZLE_128B);
+            if (rc) return rc;
+        }
     const int kg = a.kg;
-    const uintptr_t sb_addr = reinterpret_cast<uintptr_t>(a.s) | reinterpret_cast<uintptr_t>(a.b);
+    uintptr_t sb_addr = 0;
+    for (int m = 0; m < NMAT; ++m)
+        sb_addr |= reinterpret_cast<uintptr_t>(a.s[m]) | reinterpret_cast<uintptr_t>(a.b[m]);
     a.sb_vec = (kg % 8 == 0 && sb_addr % 16 == 0) ? 16 : (kg % 4 == 0 && sb_addr % 8 == 0) ? 8 : 4;
 
-    auto kern = qmvq_kernel<T, MT, FR, SXA>;
+    auto kern = qmvq_kernel<T, BITS, MT, FR, NMAT, SXA>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return LQ_E_CUDA;
     cudaLaunchConfig_t cfg = {};
@@ -455,76 +540,124 @@ static int qmvq_launch_t(const void* x, const uint32_t* w, QqArgs a, int ns_req,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kern, tw[0], tw[1], a);
+    e = cudaLaunchKernelEx(&cfg, kern, tw[0], tw[1], tw[2], tw[3], a);
     return e == cudaSuccess ? LQ_OK : LQ_E_CUDA;
 }
 
-template <typename T, int MT, bool SXA>
-static int qmvq_dispatch_fr(int FR, const void* x, const uint32_t* w, const QqArgs& a, int ns, int nctas,
-                            cudaStream_t st) {
+template <typename T, int BITS, int MT, int NMAT, bool SXA>
+static int qmvq_dispatch_fr(int FR, const uint32_t* const* w, const QqArgs& a, int ns, int nctas, cudaStream_t st) {
     switch (FR) {
-        case 1: return qmvq_launch_t<T, MT, 1, SXA>(x, w, a, ns, nctas, st);
-        case 2: return qmvq_launch_t<T, MT, 2, SXA>(x, w, a, ns, nctas, st);
-        case 3: return qmvq_launch_t<T, MT, 3, SXA>(x, w, a, ns, nctas, st);
-        case 4: return qmvq_launch_t<T, MT, 4, SXA>(x, w, a, ns, nctas, st);
+        case 1: return qmvq_launch_t<T, BITS, MT, 1, NMAT, SXA>(w, a, ns, nctas, st);
+        case 2: return qmvq_launch_t<T, BITS, MT, 2, NMAT, SXA>(w, a, ns, nctas, st);
+        case 3: return qmvq_launch_t<T, BITS, MT, 3, NMAT, SXA>(w, a, ns, nctas, st);
+        case 4: return qmvq_launch_t<T, BITS, MT, 4, NMAT, SXA>(w, a, ns, nctas, st);
+        case 5:
+            if constexpr (QqFoot<BITS, NMAT>::kMaxFr >= 5) return qmvq_launch_t<T, BITS, MT, 5, NMAT, SXA>(w, a, ns, nctas, st);
+            return LQ_E_SHAPE;
+        case 6:
+            if constexpr (QqFoot<BITS, NMAT>::kMaxFr >= 6) return qmvq_launch_t<T, BITS, MT, 6, NMAT, SXA>(w, a, ns, nctas, st);
+            return LQ_E_SHAPE;
         default: return LQ_E_SHAPE;
     }
 }
 
-template <typename T, int MT>
-static int qmvq_dispatch_sx(bool sxa, int FR, const void* x, const uint32_t* w, const QqArgs& a, int ns, int nctas,
+// x sums by adds are built for the 4-bit single-matrix kernels only (the all-ones MMA elsewhere)
+template <typename T, int BITS, int MT, int NMAT>
+static int qmvq_dispatch_sx(bool sxa, int FR, const uint32_t* const* w, const QqArgs& a, int ns, int nctas,
                             cudaStream_t st) {
-    return sxa ? qmvq_dispatch_fr<T, MT, true>(FR, x, w, a, ns, nctas, st)
-               : qmvq_dispatch_fr<T, MT, false>(FR, x, w, a, ns, nctas, st);
+    if constexpr (BITS == 4 && NMAT == 1)
+        if (sxa) return qmvq_dispatch_fr<T, BITS, MT, NMAT, true>(FR, w, a, ns, nctas, st);
+    return qmvq_dispatch_fr<T, BITS, MT, NMAT, false>(FR, w, a, ns, nctas, st);
 }
 
-bool qmvq_shape_ok(int M, int K, int bits) { return bits == 4 && M >= 1 && M <= 16 && K >= 256 && K % 256 == 0; }
+template <typename T, int NMAT>
+static int qmvq_dispatch(int bits, int M, bool sxa, int FR, const uint32_t* const* w, const QqArgs& a, int ns,
+                         int nctas, cudaStream_t st) {
+    if (bits == 4)
+        return M <= 8 ? qmvq_dispatch_sx<T, 4, 1, NMAT>(sxa, FR, w, a, ns, nctas, st)
+                      : qmvq_dispatch_sx<T, 4, 2, NMAT>(sxa, FR, w, a, ns, nctas, st);
+    return M <= 8 ? qmvq_dispatch_sx<T, 8, 1, NMAT>(sxa, FR, w, a, ns, nctas, st)
+                  : qmvq_dispatch_sx<T, 8, 2, NMAT>(sxa, FR, w, a, ns, nctas, st);
+}
 
-// p = {FR (max fragments a CTA, 0 = spread over every SM), NS (stages, 0 = choose), LOADER (weights: 0 = choose,
-// 1 = TMA by the producer warp, 2 = cp.async by the consumer threads), SX (group x sums: 0 = choose, 1 = by an
-// all-ones MMA, 2 = by fp32 adds and shuffles)}.
-int qmvq_run(const void* x, const uint32_t* w, const void* s, const void* b, int nout, void* const* outs,
-             const int* seg_end, const int* ldo, int M, int N, int K, int dtype, const int* p, cudaStream_t st) {
-    if (!qmvq_shape_ok(M, K, 4) || N < 1) return LQ_E_SHAPE;
+bool qmvq_shape_ok(int M, int K, int bits) {
+    return (bits == 4 || bits == 8) && M >= 1 && M <= 16 && K >= 256 && K % 256 == 0;
+}
+
+// The grid and fragment count of a call: CTAs of at most fr units each (0 = spread over every SM); every CTA then
+// holds FR or FR - 1 units with FR = ceil(units / nctas), the two weight-box heights the kernel is given.
+static int qmvq_grid(int units, int fr_req, int max_fr, int* nctas) {
+    const int sms = device_info().sm_count;
+    int fr = fr_req;
+    if (fr == 0) {
+        fr = (units + sms - 1) / sms;
+        if (fr > max_fr) fr = max_fr;
+    }
+    int n = (units + fr - 1) / fr;
+    if (fr_req == 0 && n < sms) n = units < sms ? units : sms;
+    *nctas = n;
+    return (units + n - 1) / n;
+}
+
+static int qmvq_common(int nmat, const void* x, const uint32_t* const* w, const void* const* s, const void* const* b,
+                       int nout, void* const* outs, const int* seg_end, const int* ldo, int M, int N, int K, int bits,
+                       int dtype, const int* p, cudaStream_t st) {
+    if (!qmvq_shape_ok(M, K, bits) || N < 1) return LQ_E_SHAPE;
     QqArgs a = {};
     a.M = M;
     a.N = N;
     a.K = K;
     a.kg = K / 64;
     a.nchunk = (K + 511) / 512;
-    a.nfrag = (N + 15) / 16;
-    a.s = s;
-    a.b = b;
+    a.units = (N + 15) / 16;
+    a.x = x;
+    for (int m = 0; m < nmat; ++m) {
+        a.s[m] = s[m];
+        a.b[m] = b[m];
+    }
     for (int i = 0; i < nout; ++i) {
         a.out[i] = outs[i];
         a.seg_end[i] = seg_end[i];
         a.ldo[i] = ldo[i];
     }
     a.nseg_out = nout;
-    const int sms = device_info().sm_count;
     const int fr_req = p ? p[0] : 0;
     const int ns = p ? p[1] : 0;
-    const int ldm = p ? p[2] : 0;
     const int sxm = p ? p[3] : 0;
-    if (fr_req < 0 || fr_req > QQ_MAX_FR || ns < 0 || ldm < 0 || ldm > 2 || sxm < 0 || sxm > 2) return LQ_E_ARG;
-    a.cpw = ldm == 2 ? 1 : 0;
-    const bool sxa = sxm == 2;
-    // CTAs: at most fr fragments each; the library's choice spreads them over every SM. Then every CTA holds FR or
-    // FR - 1 fragments with FR = ceil(nfrag / nctas), the two weight-box heights the kernel is given.
-    int fr = fr_req;
-    if (fr == 0) {
-        fr = (a.nfrag + sms - 1) / sms;
-        if (fr > QQ_MAX_FR) fr = QQ_MAX_FR;
-    }
-    int nctas = (a.nfrag + fr - 1) / fr;
-    if (fr_req == 0 && nctas < sms) nctas = a.nfrag < sms ? a.nfrag : sms;
-    const int FR = (a.nfrag + nctas - 1) / nctas;
-    const bool bf16 = dtype == LQ_BF16;
-    if (M <= 8)
-        return bf16 ? qmvq_dispatch_sx<__nv_bfloat16, 1>(sxa, FR, x, w, a, ns, nctas, st)
-                    : qmvq_dispatch_sx<__half, 1>(sxa, FR, x, w, a, ns, nctas, st);
-    return bf16 ? qmvq_dispatch_sx<__nv_bfloat16, 2>(sxa, FR, x, w, a, ns, nctas, st)
-                : qmvq_dispatch_sx<__half, 2>(sxa, FR, x, w, a, ns, nctas, st);
+    const int max_fr = (bits == 4 && nmat == 1) ? QqFoot<4, 1>::kMaxFr : QqFoot<8, 1>::kMaxFr;
+    if (fr_req < 0 || fr_req > max_fr || ns < 0 || (p && p[2] != 0) || sxm < 0 || sxm > 2) return LQ_E_ARG;
+    int nctas = 0;
+    const int FR = qmvq_grid(a.units, fr_req, max_fr, &nctas);
+    if (FR > max_fr) return LQ_E_SHAPE;
+    const bool bf16 = dtype == LQ_BF16, sxa = sxm == 2;
+    if (nmat == 1)
+        return bf16 ? qmvq_dispatch<__nv_bfloat16, 1>(bits, M, sxa, FR, w, a, ns, nctas, st)
+                    : qmvq_dispatch<__half, 1>(bits, M, sxa, FR, w, a, ns, nctas, st);
+    return bf16 ? qmvq_dispatch<__nv_bfloat16, 2>(bits, M, sxa, FR, w, a, ns, nctas, st)
+                : qmvq_dispatch<__half, 2>(bits, M, sxa, FR, w, a, ns, nctas, st);
+}
+
+// p = {FR (max units a CTA, 0 = spread over every SM), NS (stages, 0 = choose), 0, SX (group x sums: 0 = choose,
+// 1 = by an all-ones MMA, 2 = by fp32 adds and shuffles, 4-bit only)}.
+int qmvq_run(const void* x, const uint32_t* w, const void* s, const void* b, int nout, void* const* outs,
+             const int* seg_end, const int* ldo, int M, int N, int K, int bits, int dtype, const int* p,
+             cudaStream_t st) {
+    const uint32_t* ws[2] = {w, w};
+    const void* ss[2] = {s, s};
+    const void* bs[2] = {b, b};
+    return qmvq_common(1, x, ws, ss, bs, nout, outs, seg_end, ldo, M, N, K, bits, dtype, p, st);
+}
+
+// h (M, I) = swiglu(x . gate^T, x . up^T) with the rounding points of locals/moe.py:284-289.
+int qmvq_glu_run(const void* x, const uint32_t* w_gate, const void* s_gate, const void* b_gate, const uint32_t* w_up,
+                 const void* s_up, const void* b_up, void* h, int M, int I, int K, int bits, int dtype, const int* p,
+                 cudaStream_t st) {
+    const uint32_t* ws[2] = {w_gate, w_up};
+    const void* ss[2] = {s_gate, s_up};
+    const void* bs[2] = {b_gate, b_up};
+    void* outs[1] = {h};
+    const int seg_end[1] = {I}, ldo[1] = {I};
+    return qmvq_common(2, x, ws, ss, bs, 1, outs, seg_end, ldo, M, I, K, bits, dtype, p, st);
 }
 
 }  // namespace lq
