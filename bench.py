@@ -556,7 +556,7 @@ def run_gpu(args):
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample}
 
     if rank == 0:
-        traffic = profile_traffic("qmvg_fused_qkv_m16")
+        traffic = profile_traffic("qmvq_fused_qkv_m16")
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
@@ -570,7 +570,7 @@ def run_gpu(args):
                        "graph": "CUDA graph of the step, PDL between launches"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "traffic": traffic,
-                         "kernel": "lq::qmvg_kernel<bf16,MT=2,FR=3>", "peak_kind": peak_kind,
+                         "kernel": "lq::qmvq_kernel<bf16,BITS=4,MT=2,FR=3,NMAT=1>", "peak_kind": peak_kind,
                          "algorithmic_bytes_per_launch": per_launch_bytes},
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": head["h2d"],
                     "d2h_bytes_per_step": head["d2h"]},
@@ -592,8 +592,8 @@ def run_gpu(args):
 
 CASES = {
     "qkv16": "fused QKV decode, x bf16 [16,2560] . 4-bit [6144,2560]^T, 8 distinct layers (72 MB)",
-    "qkv16_l2": "fused QKV decode at M=16 (the library's choice, qmvg) over 24 layers (218 MB > L2), for DRAM figures",
-    "qkv1_l2": "fused QKV decode at M=1 (the group-per-warp qmvg kernel) over 24 layers (218 MB > L2)",
+    "qkv16_l2": "fused QKV decode at M=16 (the library's choice, qmvq) over 24 layers (218 MB > L2), for DRAM figures",
+    "qkv1_l2": "fused QKV decode at M=1 (the library's choice, qmvq) over 24 layers (218 MB > L2)",
     "mlp64": "8-bit MLP gate||up + SiLU.mul and down at M=64, 4 layers",
     "mlp1": "8-bit MLP gate||up + SiLU.mul and down at M=1, 4 layers (320 MB > L2)",
     "tc": "prefill GEMM x bf16 [1024,4096] . 4-bit [7168,4096]^T",
