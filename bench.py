@@ -459,11 +459,49 @@ def bench_sharded(torch, dist, ws, steps, warmup, dev, stream):
         out["cfg4_moe_ep"][f"M={M}"] = {"us_per_layer": round(ms * 1e3, 2), "tok/s": round(M / (ms * 1e-3), 1)}
     del ep
     gen.manual_seed(4)
-    lin = ColumnShardedLinear(QuantizedLinear(*make_layer(torch, 14336, 4096, 4, torch.bfloat16, gen, dev)))
+    full = QuantizedLinear(*make_layer(torch, 14336, 4096, 4, torch.bfloat16, gen, dev))
+    lin = ColumnShardedLinear(full)  # the GEMM stores its output tiles into every rank's buffer (fused all-gather)
+    lin_nccl = ColumnShardedLinear(full, fused_gather=False)  # the same GEMM, then an NCCL all-gather
+    del full
     x = torch.randn((2048, 4096), generator=gen, device=dev).to(torch.bfloat16)
     ms = _timed_max(torch, lambda: lin(x), max(3, steps // 4), warmup, stream, dist)
-    out["cfg5_prefill_sharded"] = {"ms": round(ms, 3), "TFLOP/s": round(2 * 2048 * 14336 * 4096 / (ms * 1e-3) / 1e12, 1)}
+    ms_nccl = _timed_max(torch, lambda: lin_nccl(x), max(3, steps // 4), warmup, stream, dist)
+    fl = 2 * 2048 * 14336 * 4096
+    out["cfg5_prefill_sharded"] = {"ms": round(ms, 3), "TFLOP/s": round(fl / (ms * 1e-3) / 1e12, 1),
+                                   "form": "dense GEMM with the all-gather in its epilogue (peer stores over NVLink)",
+                                   "nccl_allgather_ms": round(ms_nccl, 3),
+                                   "nccl_allgather_TFLOP/s": round(fl / (ms_nccl * 1e-3) / 1e12, 1)}
     return out
+
+
+def sharded_speedups(extra, ws):
+    """Per-N speed-up of each sharded configuration over the same workload on one GPU (rank 0's own runs in this
+    process): time on one GPU / time on ws GPUs, and that over ws (the parallel efficiency)."""
+    def put(key, t1, tn):
+        if t1 and tn:
+            extra[key]["speedup_vs_1gpu"] = round(t1 / tn, 3)
+            extra[key]["efficiency"] = round(t1 / tn / ws, 3)
+
+    try:
+        put("cfg5_prefill_sharded", extra["cfg5_prefill"]["ms"], extra["cfg5_prefill_sharded"]["ms"])
+    except KeyError:
+        pass
+    for M in (1, 16, 64):
+        try:
+            t1 = extra["cfg3_mlp_8bit"][f"M={M}"]["us_per_mlp"]
+            d = extra["cfg3_mlp_8bit_sharded"][f"M={M}"]
+            d["speedup_vs_1gpu"] = round(t1 / d["us_per_mlp"], 3)
+            d["efficiency"] = round(t1 / d["us_per_mlp"] / ws, 3)
+        except KeyError:
+            pass
+    for M in (8, 64, 512):
+        try:
+            t1 = extra["cfg4_moe"][f"M={M}"]["us_per_layer"]
+            d = extra["cfg4_moe_ep"][f"M={M}"]
+            d["speedup_vs_1gpu"] = round(t1 / d["us_per_layer"], 3)
+            d["efficiency"] = round(t1 / d["us_per_layer"] / ws, 3)
+        except KeyError:
+            pass
 
 
 def run_gpu(args):
@@ -549,6 +587,8 @@ def run_gpu(args):
 
     if ws > 1 and not args.quick:
         extra.update(bench_sharded(torch, dist, ws, max(5, args.steps // 2), args.warmup, dev, stream))
+        if rank == 0:
+            sharded_speedups(extra, ws)
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:

@@ -210,6 +210,25 @@ int lq_kv_attend_noalloc(const void* q, const uint32_t* kq, const void* ks, cons
                          const void* vs, const void* vb, const int32_t* start, int n, const float* sinks, float scale,
                          int B, int H, int KVH, int cap, int head_dim, int dtype, void* out, void* stream);
 
+/* The column-sharded prefill with its all-gather in the GEMM's own stores: this rank's N output columns of
+ * y = x . dequant(w)^T (the dense path of lq_qmm_dense) are stored at columns [col_off, col_off + N) of each of the
+ * ndst (<= 8) row-major (M, ldo) buffers dst[] -- this GPU's and its peers' (pointers from lq_ipc_import): one kernel
+ * computes the slice and sends it over NVLink, with no separate all-gather and no strided copy afterwards. The caller
+ * orders completion across ranks (a collective after the call) before any rank reads the buffers. No counterpart in
+ * the reference, which runs on one GPU; it replaces the all-gather that follows a column-sharded
+ * kernels._dense_matmul (locals/kernels.py:1020-1025). */
+int lq_qmm_dense_gather(const void* x, const uint32_t* w, const void* scales, const void* biases, void* const* dst,
+                        int ndst, int col_off, int ldo, int M, int N, int K, int bits, int group_size, int dtype,
+                        void* workspace, size_t workspace_bytes, const lq_cfg* cfg, void* stream);
+
+/* CUDA IPC for peer buffers between the processes of one node (no counterpart in the reference): export writes the
+ * 64-byte handle of the allocation that holds ptr and ptr's offset in it; import maps a peer's allocation into this
+ * process for the current device (peer access enabled on first use) and returns the address of the peer's ptr;
+ * close unmaps it. */
+int lq_ipc_export(const void* ptr, void* handle, size_t* offset);
+int lq_ipc_import(const void* handle, size_t offset, void** ptr);
+int lq_ipc_close(void* ptr, size_t offset);
+
 /* 1 if kernel family `family` (LQ_FAM_*; LQ_FAM_AUTO = any) accepts this shape and format, else 0. Host-only,
  * needs no GPU. Replaces the per-family supported(M, K, N, cfg) predicates the reference's tuner filters
  * its candidates with (locals/qmv_frag.py:162,519; locals/nax_kernel.py:399-408; locals/kernels.py:654-674). */

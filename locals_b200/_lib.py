@@ -47,6 +47,11 @@ SIGNATURES = {
     "lq_qmm_dense": ([_vp, _u32p, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, ctypes.c_size_t, ctypes.POINTER(Cfg), _vp],
                      _i),
     "lq_qmm_dense_workspace": ([_i, _i], ctypes.c_size_t),
+    "lq_qmm_dense_gather": ([_vp, _u32p, _vp, _vp, ctypes.POINTER(ctypes.c_void_p), _i, _i, _i, _i, _i, _i, _i, _i, _i,
+                             _vp, ctypes.c_size_t, ctypes.POINTER(Cfg), _vp], _i),
+    "lq_ipc_export": ([_vp, _vp, ctypes.POINTER(ctypes.c_size_t)], _i),
+    "lq_ipc_import": ([_vp, ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)], _i),
+    "lq_ipc_close": ([_vp, ctypes.c_size_t], _i),
     "lq_kv_attend_noalloc": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, ctypes.c_float, _i, _i, _i, _i, _i, _i,
                               _vp, _vp], _i),
     "lq_supported": ([_i, _i, _i, _i, _i, _i, _i], _i),

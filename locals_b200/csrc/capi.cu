@@ -41,6 +41,9 @@ int tcvp_run_grouped(const void* xs, int P, const QmvMats& mats, int nmat, int N
                      int ntok, cudaStream_t st);
 bool norm_shape_ok(int D);
 size_t qmm_dense_workspace_bytes(int N, int K);
+int qmm_dense_gather_run(const void* x, const uint32_t* w, const void* s, const void* b, void* const* dst, int ndst,
+                         int col_off, int ldo, int M, int N, int K, int bits, int dtype, void* workspace, const int* p,
+                         cudaStream_t st);
 bool qmm_dense_shape_ok(int M, int N, int K, int bits);
 int qmm_dense_run(const void* x, const uint32_t* w, const void* s, const void* b, void* y, int M, int N, int K,
                   int bits, int dtype, void* workspace, const int* p, cudaStream_t st);
@@ -452,6 +455,65 @@ int lq_qmm_dense(const void* x, const uint32_t* w, const void* scales, const voi
     return finish(qmm_dense_run(x, w, scales, biases, y, M, N, K, bits, dtype, workspace,
                                 (cfg && cfg->family == LQ_FAM_TC) ? cfg->p : nullptr,
                                 reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int lq_qmm_dense_gather(const void* x, const uint32_t* w, const void* scales, const void* biases, void* const* dst,
+                        int ndst, int col_off, int ldo, int M, int N, int K, int bits, int group_size, int dtype,
+                        void* workspace, size_t workspace_bytes, const lq_cfg* cfg, void* stream) {
+    int rc = check_common(x, w, scales, biases, M, N, K, bits, group_size, dtype);
+    if (rc) return rc;
+    if (!dst || !workspace || ndst < 1 || ndst > 8 || col_off < 0 || ldo < col_off + N) return LQ_E_ARG;
+    for (int d = 0; d < ndst; ++d)
+        if (!dst[d]) return LQ_E_ARG;
+        else if (!aligned(dst[d], 16)) return LQ_E_ALIGN;
+    if (!qmm_dense_shape_ok(M, N, K, bits)) return LQ_E_SHAPE;
+    if (workspace_bytes < qmm_dense_workspace_bytes(N, K)) return LQ_E_ARG;
+    if (!aligned(workspace, 16) || (bits == 4 && (!aligned(scales, 2) || !aligned(biases, 2)))) return LQ_E_ALIGN;
+    rc = check_device();
+    if (rc) return rc;
+    return finish(qmm_dense_gather_run(x, w, scales, biases, dst, ndst, col_off, ldo, M, N, K, bits, dtype, workspace,
+                                       (cfg && cfg->family == LQ_FAM_TC) ? cfg->p : nullptr,
+                                       reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int lq_ipc_export(const void* ptr, void* handle, size_t* offset) {
+    if (!ptr || !handle || !offset) return LQ_E_ARG;
+    const void* base = nullptr;
+    int rc = alloc_base(ptr, &base);
+    if (rc) return rc;
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(base));
+    if (e != cudaSuccess) {
+        note_cuda_error(e);
+        return LQ_E_CUDA;
+    }
+    memcpy(handle, &h, sizeof(h));
+    *offset = size_t(reinterpret_cast<const uint8_t*>(ptr) - reinterpret_cast<const uint8_t*>(base));
+    return LQ_OK;
+}
+
+int lq_ipc_import(const void* handle, size_t offset, void** ptr) {
+    if (!handle || !ptr) return LQ_E_ARG;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    void* base = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+        note_cuda_error(e);
+        return LQ_E_CUDA;
+    }
+    *ptr = static_cast<uint8_t*>(base) + offset;
+    return LQ_OK;
+}
+
+int lq_ipc_close(void* ptr, size_t offset) {
+    if (!ptr) return LQ_E_ARG;
+    const cudaError_t e = cudaIpcCloseMemHandle(static_cast<uint8_t*>(ptr) - offset);
+    if (e != cudaSuccess) {
+        note_cuda_error(e);
+        return LQ_E_CUDA;
+    }
+    return LQ_OK;
 }
 
 size_t lq_kv_attend_workspace(int B, int H, int KVH, int n) {

@@ -36,6 +36,31 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
+typedef CUresult (*AddrRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+static AddrRangeFn addr_range_fn() {
+    static AddrRangeFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<AddrRangeFn>(p);
+    });
+    return fn;
+}
+
+int alloc_base(const void* ptr, const void** base) {
+    AddrRangeFn fn = addr_range_fn();
+    if (!fn) return LQ_E_CUDA;
+    CUdeviceptr b = 0;
+    size_t size = 0;
+    if (fn(&b, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return LQ_E_ARG;
+    *base = reinterpret_cast<const void*>(b);
+    return LQ_OK;
+}
+
 int make_tmap(CUtensorMap* out, CUtensorMapDataType dt, int rank, const void* base, const uint64_t* dims,
               const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle) {
     if (reinterpret_cast<uintptr_t>(base) % 16) return LQ_E_ALIGN;

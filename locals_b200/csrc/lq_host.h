@@ -16,6 +16,9 @@ namespace lq {
 int make_tmap(CUtensorMap* out, CUtensorMapDataType dt, int rank, const void* base, const uint64_t* dims,
               const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle);
 
+// The start of the device allocation that holds ptr (LQ_E_ARG if ptr is not device memory of this process).
+int alloc_base(const void* ptr, const void** base);
+
 struct DeviceInfo {
     int device = -1;
     int sm_count = 0;

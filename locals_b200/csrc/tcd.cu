@@ -97,10 +97,16 @@ struct TcdShape {
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
 };
 
+constexpr int TCD_MAX_DST = 8;
+
 struct TcdArgs {
     int M, N, K, nk;
     int mt, ntiles;  // token tiles, all tiles
     void* y;
+    // Column-sharded gather: ndst > 0 stores every output element at column col_off + n of row m (leading dimension
+    // ldo) in each of the ndst buffers dst[] -- this GPU's and its peers' (P2P pointers) -- instead of y.
+    int ndst, col_off, ldo;
+    void* dst[TCD_MAX_DST];
 };
 
 template <typename T, int BN>
@@ -200,7 +206,9 @@ __global__ void __launch_bounds__(TCD_THREADS, 1)
         }
     } else {
         // ------------------------------ epilogue warps 0-3 ------------------------------
-        const bool vec = (a.N & 7) == 0;
+        const int ndst = a.ndst > 0 ? a.ndst : 1;
+        const int ldo = a.ndst > 0 ? a.ldo : a.N, col_off = a.ndst > 0 ? a.col_off : 0;
+        const bool vec = ((a.N | ldo | col_off) & 7) == 0;
         for (int j = 0; j < my_tiles; ++j) {
             const int buf = j & 1;
             const int tile = int(blockIdx.x) + j * int(gridDim.x);
@@ -209,7 +217,7 @@ __global__ void __launch_bounds__(TCD_THREADS, 1)
             if (!ok) break;
             tc_fence_after();
             const int m = m0 + 32 * warp + lane;
-            T* yrow = reinterpret_cast<T*>(a.y) + size_t(m) * a.N;
+            const size_t row_off = size_t(m) * ldo + col_off;
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 uint32_t r[32];
@@ -224,15 +232,21 @@ __global__ void __launch_bounds__(TCD_THREADS, 1)
 #pragma unroll
                     for (int q = 0; q < 4; ++q)
                         o[q] = TR::pack2(__uint_as_float(r[8 * v + 2 * q + 1]), __uint_as_float(r[8 * v + 2 * q]));
-                    if (vec && nn + 8 <= a.N) {
-                        *reinterpret_cast<uint4*>(yrow + nn) = make_uint4(o[0], o[1], o[2], o[3]);
-                    } else {
-                        for (int q = 0; q < 8; ++q)
-                            if (nn + q < a.N) {
-                                const uint32_t word = o[q >> 1];
-                                reinterpret_cast<uint16_t*>(yrow)[nn + q] =
-                                    (q & 1) ? uint16_t(word >> 16) : uint16_t(word & 0xFFFF);
-                            }
+                    // every destination (this GPU's y, or each rank's gathered output: peers over NVLink)
+#pragma unroll
+                    for (int d = 0; d < TCD_MAX_DST; ++d) {
+                        if (d >= ndst) break;
+                        T* yrow = reinterpret_cast<T*>(a.ndst > 0 ? a.dst[d] : a.y) + row_off;
+                        if (vec && nn + 8 <= a.N) {
+                            *reinterpret_cast<uint4*>(yrow + nn) = make_uint4(o[0], o[1], o[2], o[3]);
+                        } else {
+                            for (int q = 0; q < 8; ++q)
+                                if (nn + q < a.N) {
+                                    const uint32_t word = o[q >> 1];
+                                    reinterpret_cast<uint16_t*>(yrow)[nn + q] =
+                                        (q & 1) ? uint16_t(word >> 16) : uint16_t(word & 0xFFFF);
+                                }
+                        }
                     }
                 }
             }
@@ -240,6 +254,7 @@ __global__ void __launch_bounds__(TCD_THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
+        if (a.ndst > 0) __threadfence_system();  // the peer stores are visible system-wide before the kernel ends
     }
     tc_fence_before();
     __syncthreads();
@@ -287,9 +302,11 @@ static int dequant4_launch(const uint32_t* w, const void* s, const void* b, int 
 }
 
 template <typename T, int BN>
-static int tcd_launch_t(const void* x, const void* wd, void* y, int M, int N, int K, cudaStream_t st) {
+static int tcd_launch_t(const void* x, const void* wd, void* y, int M, int N, int K, const TcdArgs* gather,
+                        cudaStream_t st) {
     using S = TcdShape<BN>;
-    TcdArgs a;
+    TcdArgs a = {};
+    if (gather) a = *gather;
     a.M = M;
     a.N = N;
     a.K = K;
@@ -331,9 +348,8 @@ bool qmm_dense_shape_ok(int M, int N, int K, int bits) {
 int dequantize_run(const uint32_t* wq, const void* s, const void* b, int N, int K, int bits, int group, int dt,
                    void* out, cudaStream_t st);
 
-// p = {BN (0 = 224 when that divides N, else 256)}. workspace: N x K weights in the activation dtype.
-int qmm_dense_run(const void* x, const uint32_t* w, const void* s, const void* b, void* y, int M, int N, int K,
-                  int bits, int dtype, void* workspace, const int* p, cudaStream_t st) {
+static int qmm_dense_impl(const void* x, const uint32_t* w, const void* s, const void* b, void* y, int M, int N, int K,
+                          int bits, int dtype, void* workspace, const int* p, const TcdArgs* gather, cudaStream_t st) {
     const bool bf16 = dtype == LQ_BF16;
     int rc;
     if (bits == 4)
@@ -346,12 +362,35 @@ int qmm_dense_run(const void* x, const uint32_t* w, const void* s, const void* b
     if (bn == 0) bn = (N % 224 == 0) ? 224 : 256;
 #define LQ_TCD_CASE(BN_) \
     if (bn == BN_)       \
-        return bf16 ? tcd_launch_t<__nv_bfloat16, BN_>(x, workspace, y, M, N, K, st) : tcd_launch_t<__half, BN_>(x, workspace, y, M, N, K, st);
+        return bf16 ? tcd_launch_t<__nv_bfloat16, BN_>(x, workspace, y, M, N, K, gather, st) : tcd_launch_t<__half, BN_>(x, workspace, y, M, N, K, gather, st);
     LQ_TCD_CASE(256)
     LQ_TCD_CASE(224)
     LQ_TCD_CASE(128)
 #undef LQ_TCD_CASE
     return LQ_E_ARG;
+}
+
+// p = {BN (0 = 224 when that divides N, else 256)}. workspace: N x K weights in the activation dtype.
+int qmm_dense_run(const void* x, const uint32_t* w, const void* s, const void* b, void* y, int M, int N, int K,
+                  int bits, int dtype, void* workspace, const int* p, cudaStream_t st) {
+    return qmm_dense_impl(x, w, s, b, y, M, N, K, bits, dtype, workspace, p, nullptr, st);
+}
+
+// The column-sharded form: this rank's N output columns go to columns [col_off, col_off + N) of the (M, ldo) buffers
+// dst[0 .. ndst) (one a rank: the all-gather done by the GEMM's own stores).
+int qmm_dense_gather_run(const void* x, const uint32_t* w, const void* s, const void* b, void* const* dst, int ndst,
+                         int col_off, int ldo, int M, int N, int K, int bits, int dtype, void* workspace, const int* p,
+                         cudaStream_t st) {
+    if (ndst < 1 || ndst > TCD_MAX_DST || col_off < 0 || ldo < col_off + N) return LQ_E_ARG;
+    TcdArgs g = {};
+    g.ndst = ndst;
+    g.col_off = col_off;
+    g.ldo = ldo;
+    for (int d = 0; d < ndst; ++d) {
+        if (!dst[d]) return LQ_E_ARG;
+        g.dst[d] = dst[d];
+    }
+    return qmm_dense_impl(x, w, s, b, dst[0], M, N, K, bits, dtype, workspace, p, &g, st);
 }
 
 }  // namespace lq

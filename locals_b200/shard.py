@@ -5,7 +5,10 @@ The reference runs one model on one Apple GPU and has no distributed code; the p
 * ``ColumnShardedLinear`` -- a quantized linear split by output rows (columns of y): rank r keeps rows
   [r N/G, (r+1) N/G) of the packed weights, scales and biases (quantization groups run along K, so each
   row block is itself a valid MLX-format matrix, the argument of locals/fuse.py:3-6), computes its slice
-  of y with the decode or prefill kernel and NCCL all-gathers the slices.
+  of y with the decode or prefill kernel and NCCL all-gathers the slices. Prefill-size calls (the dense
+  dequantize + tcgen05 GEMM path) fuse the all-gather into the GEMM: its epilogue stores each output tile into
+  every rank's full (M, N) buffer over NVLink (``PeerOutputs``: buffers mapped into every rank's process by CUDA
+  IPC), and one small NCCL all-reduce orders completion -- no NCCL all-gather, no strided copy.
 * ``ShardedQKV`` -- the fused q/k/v projection split at head boundaries: rank r keeps H/G query heads and
   KVH/G key/value heads; its local q/k/v come out of one kernel, then are all-gathered into full q, k, v.
 * ``ShardedMLP`` -- gate||up split by intermediate rows (the SwiGLU is row-local), h all-gathered, the down
@@ -29,6 +32,10 @@ import torch
 import torch.distributed as dist
 
 from .kernels import QuantizedLinear
+
+# the fused GEMM + all-gather needs the dense prefill path and stores to at most this many ranks
+FUSED_GATHER_MIN_M = 128
+FUSED_GATHER_MAX_RANKS = 8
 
 
 def _world(group) -> tuple:
@@ -97,17 +104,107 @@ def all_gather_cols(y_local: torch.Tensor, group=None) -> torch.Tensor:
     return buf.view(G, M, Nl).permute(1, 0, 2).reshape(M, G * Nl)
 
 
+class PeerOutputs:
+    """Two (M, N) output buffers of this rank (used in turn), mapped into every rank's process through CUDA IPC
+    (handles exchanged over the process group), so a kernel on any rank can store into any rank's buffer. Creating
+    one is a collective: every rank creates it with the same shape in the same order. A buffer handed out by
+    ``next`` is overwritten two calls later: its readers must be queued on the stream before then."""
+
+    def __init__(self, shape, dtype, device, group=None):
+        import ctypes
+
+        from . import _lib
+
+        G, r = _world(group)
+        self.G, self.rank = G, r
+        M, N = shape
+        self.block = torch.empty((2, M, N), dtype=dtype, device=device)  # one allocation: one IPC handle
+        h = (ctypes.c_char * 64)()
+        off = ctypes.c_size_t()
+        _lib.call("lq_ipc_export", self.block.data_ptr(), h, ctypes.byref(off))
+        handles = [None] * G
+        dist.all_gather_object(handles, (bytes(h), int(off.value)), group=group)
+        self.bases = []  # every rank's block, as an address valid in this process
+        self._opened = []
+        for p, (hb, o) in enumerate(handles):
+            if p == r:
+                self.bases.append(self.block.data_ptr())
+                continue
+            ptr = ctypes.c_void_p()
+            _lib.call("lq_ipc_import", (ctypes.c_char * 64).from_buffer_copy(hb), o, ctypes.byref(ptr))
+            self.bases.append(int(ptr.value))
+            self._opened.append((int(ptr.value), o))
+        self.step = M * N * self.block.element_size()
+        self.i = 0
+
+    def next(self):
+        """(this rank's buffer, every rank's address of that buffer)."""
+        j = self.i
+        self.i ^= 1
+        return self.block[j], [b + j * self.step for b in self.bases]
+
+    def close(self) -> None:
+        import ctypes
+
+        from . import _lib
+
+        for ptr, o in self._opened:
+            _lib.lib().lq_ipc_close(ctypes.c_void_p(ptr), o)
+        self._opened = []
+
+
 class ColumnShardedLinear:
-    def __init__(self, full: QuantizedLinear, group=None, ops: Optional[Ops] = None):
+    def __init__(self, full: QuantizedLinear, group=None, ops: Optional[Ops] = None, fused_gather: bool = True):
         self.group = group
         G, r = _world(group)
         self.G, self.rank = G, r
+        self.N = full.weight.shape[0]
         self.local = QuantizedLinear(_split_rows(full.weight, G, r), _split_rows(full.scales, G, r),
                                      _split_rows(full.biases, G, r), full.bits, full.group_size)
         self.ops = ops or kernel_ops()
+        self.fused_gather = fused_gather and ops is None
+        self._peer = {}
+        self._flag = None
+
+    def _fused_ok(self, x2: torch.Tensor) -> bool:
+        from . import kernels
+
+        M, K = x2.shape
+        Nl = self.local.weight.shape[0]
+        return (self.fused_gather and 1 < self.G <= FUSED_GATHER_MAX_RANKS and x2.is_cuda and M >= FUSED_GATHER_MIN_M
+                and self.local.group_size == 64 and self.local.bits in (4, 8) and K % 64 == 0
+                and Nl * K <= kernels.DENSE_MAX and (self.rank * Nl) % 8 == 0 and self.N % 8 == 0)
+
+    def _gather_dense(self, x2: torch.Tensor) -> torch.Tensor:
+        """The dense GEMM of this rank's rows with the all-gather in its own stores (lq_qmm_dense_gather)."""
+        import ctypes
+
+        from . import _lib, kernels
+
+        M, K = x2.shape
+        Nl = self.local.weight.shape[0]
+        key = (M, x2.dtype)
+        if key not in self._peer:
+            self._peer[key] = PeerOutputs((M, self.N), x2.dtype, x2.device, self.group)
+            self._flag = torch.zeros(1, dtype=torch.float32, device=x2.device)
+        y, addrs = self._peer[key].next()
+        order = [(self.rank + j) % self.G for j in range(self.G)]  # each rank sends to the others in turn
+        dst = (ctypes.c_void_p * self.G)(*[addrs[p] for p in order])
+        nbytes = int(_lib.lib().lq_qmm_dense_workspace(Nl, K))
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=x2.device)  # the dequantized weight rows
+        _lib.call("lq_qmm_dense_gather", x2.data_ptr(), self.local.weight.data_ptr(), self.local.scales.data_ptr(),
+                  self.local.biases.data_ptr(), dst, self.G, self.rank * Nl, self.N, M, Nl, K, self.local.bits,
+                  self.local.group_size, kernels.dtype_code(x2.dtype), ws.data_ptr(), nbytes, None,
+                  torch.cuda.current_stream().cuda_stream)
+        dist.all_reduce(self._flag, group=self.group)  # every rank's stores are complete before any rank reads y
+        return y
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         x2 = x.reshape(-1, x.shape[-1])
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        if self._fused_ok(x2):
+            return self._gather_dense(x2).reshape(*x.shape[:-1], -1)
         y = self.ops.qmm(x2, (self.local.weight, self.local.scales, self.local.biases), self.local.bits)
         return all_gather_cols(y, self.group).reshape(*x.shape[:-1], -1)
 

@@ -45,6 +45,21 @@ def _worker(rank, world, port, path):
         x = torch.randn((8, 2048), generator=gen, device=dev).to(torch.bfloat16)
         ref = kernels.quantized_matmul(x, lin.weight, lin.scales, lin.biases)
         errs["linear"] = float((ColumnShardedLinear(lin)(x).float() - ref.float()).abs().max() / ref.float().abs().max())
+        # prefill size: the dense GEMM with the all-gather in its own stores (peer buffers by CUDA IPC), twice in a
+        # row (the two peer buffers), against the same dense path on one GPU; and the NCCL all-gather form
+        big = QuantizedLinear(*layer(1024, 2048, 4))
+        xp = torch.randn((256, 2048), generator=gen, device=dev).to(torch.bfloat16)
+        refp = kernels.quantized_matmul(xp, big.weight, big.scales, big.biases, choice=("dense",)).float()
+        fused = ColumnShardedLinear(big)
+        y1 = fused(xp).float().clone()
+        y2 = fused(xp * 2).float().clone()
+        errs["gather_fused"] = float((y1 - refp).abs().max() / refp.abs().max())
+        refp2 = kernels.quantized_matmul(xp * 2, big.weight, big.scales, big.biases, choice=("dense",)).float()
+        errs["gather_fused_2"] = float((y2 - refp2).abs().max() / refp2.abs().max())
+        errs["gather_nccl"] = float((ColumnShardedLinear(big, fused_gather=False)(xp).float() - refp).abs().max()
+                                    / refp.abs().max())
+        for pb in fused._peer.values():
+            pb.close()
         g, u, d = (QuantizedLinear(*layer(1024, 2048, 8), bits=8), QuantizedLinear(*layer(1024, 2048, 8), bits=8),
                    QuantizedLinear(*layer(2048, 1024, 8), bits=8))
         h = kernels.qmm_glu(x, (g.weight, g.scales, g.biases), (u.weight, u.scales, u.biases), bits=8)
