@@ -210,13 +210,13 @@ int lq_kv_attend_noalloc(const void* q, const uint32_t* kq, const void* ks, cons
                          const void* vs, const void* vb, const int32_t* start, int n, const float* sinks, float scale,
                          int B, int H, int KVH, int cap, int head_dim, int dtype, void* out, void* stream);
 
-/* The column-sharded prefill with its all-gather in the GEMM's own stores: this rank's N output columns of
- * y = x . dequant(w)^T (the dense path of lq_qmm_dense) are stored at columns [col_off, col_off + N) of each of the
- * ndst (<= 8) row-major (M, ldo) buffers dst[] -- this GPU's and its peers' (pointers from lq_ipc_import): one kernel
- * computes the slice and sends it over NVLink, with no separate all-gather and no strided copy afterwards. The caller
- * orders completion across ranks (a collective after the call) before any rank reads the buffers. No counterpart in
- * the reference, which runs on one GPU; it replaces the all-gather that follows a column-sharded
- * kernels._dense_matmul (locals/kernels.py:1020-1025). */
+/* The column-sharded prefill with its own all-gather: this rank's N output columns of y = x . dequant(w)^T (the
+ * dense path of lq_qmm_dense) are written by the GEMM in place at columns [col_off, col_off + N) of dst[0], this GPU's
+ * row-major (M, ldo) buffer, then copied by one kernel of plain 16-byte peer stores into the same columns of
+ * dst[1 .. ndst) (ndst <= 8; peers' buffers, pointers from lq_ipc_import) -- no staging buffer, no strided copy, no
+ * NCCL all-gather. N, col_off and ldo are multiples of 8 when ndst > 1. The caller orders completion across ranks (a
+ * collective after the call) before any rank reads its buffer. No counterpart in the reference, which runs on one
+ * GPU; it replaces the all-gather that follows a column-sharded kernels._dense_matmul (locals/kernels.py:1020-1025). */
 int lq_qmm_dense_gather(const void* x, const uint32_t* w, const void* scales, const void* biases, void* const* dst,
                         int ndst, int col_off, int ldo, int M, int N, int K, int bits, int group_size, int dtype,
                         void* workspace, size_t workspace_bytes, const lq_cfg* cfg, void* stream);

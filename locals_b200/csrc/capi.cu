@@ -463,6 +463,7 @@ int lq_qmm_dense_gather(const void* x, const uint32_t* w, const void* scales, co
     int rc = check_common(x, w, scales, biases, M, N, K, bits, group_size, dtype);
     if (rc) return rc;
     if (!dst || !workspace || ndst < 1 || ndst > 8 || col_off < 0 || ldo < col_off + N) return LQ_E_ARG;
+    if (ndst > 1 && (N % 8 || col_off % 8 || ldo % 8)) return LQ_E_ALIGN;  // 16-byte pieces for the peer copy
     for (int d = 0; d < ndst; ++d)
         if (!dst[d]) return LQ_E_ARG;
         else if (!aligned(dst[d], 16)) return LQ_E_ALIGN;

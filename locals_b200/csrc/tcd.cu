@@ -103,8 +103,8 @@ struct TcdArgs {
     int M, N, K, nk;
     int mt, ntiles;  // token tiles, all tiles
     void* y;
-    // Column-sharded gather: ndst > 0 stores every output element at column col_off + n of row m (leading dimension
-    // ldo) in each of the ndst buffers dst[] -- this GPU's and its peers' (P2P pointers) -- instead of y.
+    // Column-sharded output: ndst > 0 stores output element (m, n) at column col_off + n of row m (leading dimension
+    // ldo) of dst[0] -- this rank's slice written in place into the gathered (M, ldo) layout -- instead of y.
     int ndst, col_off, ldo;
     void* dst[TCD_MAX_DST];
 };
@@ -206,7 +206,6 @@ __global__ void __launch_bounds__(TCD_THREADS, 1)
         }
     } else {
         // ------------------------------ epilogue warps 0-3 ------------------------------
-        const int ndst = a.ndst > 0 ? a.ndst : 1;
         const int ldo = a.ndst > 0 ? a.ldo : a.N, col_off = a.ndst > 0 ? a.col_off : 0;
         const bool vec = ((a.N | ldo | col_off) & 7) == 0;
         for (int j = 0; j < my_tiles; ++j) {
@@ -232,21 +231,16 @@ __global__ void __launch_bounds__(TCD_THREADS, 1)
 #pragma unroll
                     for (int q = 0; q < 4; ++q)
                         o[q] = TR::pack2(__uint_as_float(r[8 * v + 2 * q + 1]), __uint_as_float(r[8 * v + 2 * q]));
-                    // every destination (this GPU's y, or each rank's gathered output: peers over NVLink)
-#pragma unroll
-                    for (int d = 0; d < TCD_MAX_DST; ++d) {
-                        if (d >= ndst) break;
-                        T* yrow = reinterpret_cast<T*>(a.ndst > 0 ? a.dst[d] : a.y) + row_off;
-                        if (vec && nn + 8 <= a.N) {
-                            *reinterpret_cast<uint4*>(yrow + nn) = make_uint4(o[0], o[1], o[2], o[3]);
-                        } else {
-                            for (int q = 0; q < 8; ++q)
-                                if (nn + q < a.N) {
-                                    const uint32_t word = o[q >> 1];
-                                    reinterpret_cast<uint16_t*>(yrow)[nn + q] =
-                                        (q & 1) ? uint16_t(word >> 16) : uint16_t(word & 0xFFFF);
-                                }
-                        }
+                    T* yrow = reinterpret_cast<T*>(a.ndst > 0 ? a.dst[0] : a.y) + row_off;
+                    if (vec && nn + 8 <= a.N) {
+                        *reinterpret_cast<uint4*>(yrow + nn) = make_uint4(o[0], o[1], o[2], o[3]);
+                    } else {
+                        for (int q = 0; q < 8; ++q)
+                            if (nn + q < a.N) {
+                                const uint32_t word = o[q >> 1];
+                                reinterpret_cast<uint16_t*>(yrow)[nn + q] =
+                                    (q & 1) ? uint16_t(word >> 16) : uint16_t(word & 0xFFFF);
+                            }
                     }
                 }
             }
@@ -254,7 +248,6 @@ __global__ void __launch_bounds__(TCD_THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
-        if (a.ndst > 0) __threadfence_system();  // the peer stores are visible system-wide before the kernel ends
     }
     tc_fence_before();
     __syncthreads();
@@ -376,8 +369,30 @@ int qmm_dense_run(const void* x, const uint32_t* w, const void* s, const void* b
     return qmm_dense_impl(x, w, s, b, y, M, N, K, bits, dtype, workspace, p, nullptr, st);
 }
 
-// The column-sharded form: this rank's N output columns go to columns [col_off, col_off + N) of the (M, ldo) buffers
-// dst[0 .. ndst) (one a rank: the all-gather done by the GEMM's own stores).
+// Columns [col_off, col_off + ncols) of the row-major (M, ldo) buffer src copied into the same place of each of the
+// ndst buffers dst[] (peers' buffers, P2P pointers over NVLink). One thread a 16-byte piece, consecutive threads
+// along a row: every warp store is a run of 512 contiguous bytes, which NVLink carries at full width (one row per
+// lane, as the GEMM epilogue stores, reached only a third of the link's rate on B200).
+struct PushDst {
+    uint4* p[TCD_MAX_DST];
+};
+
+__global__ void __launch_bounds__(256) push_cols_kernel_p(const uint4* __restrict__ src, const PushDst dst, int ndst,
+                                                          int M, int pieces_row, int ld_pieces, int off_pieces) {
+    grid_dep_wait();
+    const int64_t total = int64_t(M) * pieces_row;
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t m = i / pieces_row, c = i - m * pieces_row;
+        const int64_t off = m * ld_pieces + off_pieces + c;
+        const uint4 v = src[off];
+#pragma unroll
+        for (int d = 0; d < TCD_MAX_DST; ++d)
+            if (d < ndst) dst.p[d][off] = v;
+    }
+}
+
+// The column-sharded form: this rank's N output columns are written in place into columns [col_off, col_off + N)
+// of its own (M, ldo) buffer dst[0] by the GEMM, then pushed to the same columns of dst[1 .. ndst) (the peers').
 int qmm_dense_gather_run(const void* x, const uint32_t* w, const void* s, const void* b, void* const* dst, int ndst,
                          int col_off, int ldo, int M, int N, int K, int bits, int dtype, void* workspace, const int* p,
                          cudaStream_t st) {
@@ -390,7 +405,19 @@ int qmm_dense_gather_run(const void* x, const uint32_t* w, const void* s, const 
         if (!dst[d]) return LQ_E_ARG;
         g.dst[d] = dst[d];
     }
-    return qmm_dense_impl(x, w, s, b, dst[0], M, N, K, bits, dtype, workspace, p, &g, st);
+    int rc = qmm_dense_impl(x, w, s, b, dst[0], M, N, K, bits, dtype, workspace, p, &g, st);
+    if (rc || ndst == 1) return rc;
+    if ((N | col_off | ldo) % 8) return LQ_E_ALIGN;  // (16-byte pieces: the host checks before the GEMM)
+    PushDst pd = {};
+    for (int d = 1; d < ndst; ++d) pd.p[d - 1] = static_cast<uint4*>(dst[d]);
+    const uint4* src = static_cast<const uint4*>(dst[0]);
+    int nd = ndst - 1, M_ = M, pr = N / 8, ldp = ldo / 8, offp = col_off / 8;
+    const int64_t total = int64_t(M) * pr;
+    int64_t blocks = (total + 255) / 256;
+    const int64_t cap = int64_t(device_info().sm_count) * 8;
+    if (blocks > cap) blocks = cap;
+    void* args[] = {&src, &pd, &nd, &M_, &pr, &ldp, &offp};
+    return pdl_launch(reinterpret_cast<const void*>(push_cols_kernel_p), dim3(unsigned(blocks)), dim3(256), 0, st, args);
 }
 
 }  // namespace lq

@@ -6,9 +6,10 @@ The reference runs one model on one Apple GPU and has no distributed code; the p
   [r N/G, (r+1) N/G) of the packed weights, scales and biases (quantization groups run along K, so each
   row block is itself a valid MLX-format matrix, the argument of locals/fuse.py:3-6), computes its slice
   of y with the decode or prefill kernel and NCCL all-gathers the slices. Prefill-size calls (the dense
-  dequantize + tcgen05 GEMM path) fuse the all-gather into the GEMM: its epilogue stores each output tile into
-  every rank's full (M, N) buffer over NVLink (``PeerOutputs``: buffers mapped into every rank's process by CUDA
-  IPC), and one small NCCL all-reduce orders completion -- no NCCL all-gather, no strided copy.
+  dequantize + tcgen05 GEMM path) do their own all-gather: the GEMM writes its slice in place into this rank's
+  full (M, N) buffer, one copy kernel of plain peer stores puts the slice into every other rank's buffer over
+  NVLink (``PeerOutputs``: buffers mapped into every rank's process by CUDA IPC), and one small NCCL all-reduce
+  orders completion -- no NCCL all-gather, no strided copy.
 * ``ShardedQKV`` -- the fused q/k/v projection split at head boundaries: rank r keeps H/G query heads and
   KVH/G key/value heads; its local q/k/v come out of one kernel, then are all-gathered into full q, k, v.
 * ``ShardedMLP`` -- gate||up split by intermediate rows (the SwiGLU is row-local), h all-gathered, the down
@@ -176,7 +177,8 @@ class ColumnShardedLinear:
                 and Nl * K <= kernels.DENSE_MAX and (self.rank * Nl) % 8 == 0 and self.N % 8 == 0)
 
     def _gather_dense(self, x2: torch.Tensor) -> torch.Tensor:
-        """The dense GEMM of this rank's rows with the all-gather in its own stores (lq_qmm_dense_gather)."""
+        """The dense GEMM of this rank's rows written in place into the gathered layout, then pushed to the peers
+        (lq_qmm_dense_gather)."""
         import ctypes
 
         from . import _lib, kernels
@@ -188,7 +190,7 @@ class ColumnShardedLinear:
             self._peer[key] = PeerOutputs((M, self.N), x2.dtype, x2.device, self.group)
             self._flag = torch.zeros(1, dtype=torch.float32, device=x2.device)
         y, addrs = self._peer[key].next()
-        order = [(self.rank + j) % self.G for j in range(self.G)]  # each rank sends to the others in turn
+        order = [(self.rank + j) % self.G for j in range(self.G)]  # its own buffer first, then the others in turn
         dst = (ctypes.c_void_p * self.G)(*[addrs[p] for p in order])
         nbytes = int(_lib.lib().lq_qmm_dense_workspace(Nl, K))
         ws = torch.empty(nbytes, dtype=torch.uint8, device=x2.device)  # the dequantized weight rows
