@@ -615,8 +615,12 @@ int lq_list_configs(int M, int N, int K, int bits, int group_size, int dtype, lq
     }
     if (lq_supported(LQ_FAM_QMVQ, M, N, K, bits, group_size, dtype)) {
         add(LQ_FAM_QMVQ, 0, 0, 0, 0);
-        for (int sx = 1; sx <= 2; ++sx)
+        const int sxs = bits == 4 ? 2 : 1;  // (x sums by adds: 4-bit single matrices only)
+        for (int sx = 1; sx <= sxs; ++sx)
             for (int fr = 0; fr <= 4; ++fr) add(LQ_FAM_QMVQ, fr, 0, 0, sx);
+        const int kss[3] = {1, 2, 4};  // K slices over a cluster
+        for (int ks : kss)
+            if (ks <= (K + 511) / 512) add(LQ_FAM_QMVQ, 0, 0, ks, 0);
     }
     if (lq_supported(LQ_FAM_TCV, M, N, K, bits, group_size, dtype)) {
         add(LQ_FAM_TCV, 0, 0, 0, 0);

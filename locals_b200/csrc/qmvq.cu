@@ -73,6 +73,7 @@ struct QqShape {
     // lane quad writes at once 8 banks apart, so every partial-sum store of a warp is free of bank conflicts
     static constexpr int RRP = NMAT * FR * 16 + 4;
     static constexpr int RED_BYTES = QQ_CW * MTOK * RRP * 4;
+    static constexpr int PART_BYTES = NMAT * MTOK * FR * 16 * 4;  // a K slice's sums [matrix][token][FR * 16 rows]
     // x loaded DX stages ahead of its use: two for up to 8 tokens, one for 16 (the register budget)
     static constexpr int DX = MT == 1 ? 2 : 1;
     static_assert(W_FRAG % 1024 == 0, "1 KB alignment of swizzled tiles");
@@ -84,6 +85,7 @@ struct QqArgs {
     int nchunk;    // stages of 512 K values
     int units;     // 16-row fragments of each matrix (ceil(N / 16))
     int ns;        // ring depth
+    int ks;        // K slices: a thread-block cluster of ks CTAs along y shares the units, each a run of stages
     int sb_vec;    // cp.async width for scale / bias rows
     const void* x;
     const void* s[2];
@@ -201,7 +203,11 @@ __global__ void __launch_bounds__(QQ_THREADS, QqFoot<BITS, NMAT>::kMinBlocks)
         return;
     }
     const int row0 = 16 * u0;
-    const int total = a.nchunk;
+    // this CTA's K slice: stages [c0, c0 + total) of the cluster's units
+    const int ks = a.ks;
+    const int krank = ks > 1 ? int(cluster_ctarank()) : 0;
+    const int c0 = (a.nchunk * krank) / ks;
+    const int total = (a.nchunk * (krank + 1)) / ks - c0;
     const int mv = a.M < S::MTOK ? a.M : S::MTOK;  // real token rows
 
     if (threadIdx.x == 0) {
@@ -251,18 +257,19 @@ __global__ void __launch_bounds__(QQ_THREADS, QqFoot<BITS, NMAT>::kMinBlocks)
             cp_async_arrive(&full[s]);
         };
         const int pre = total < ns ? total : ns;
-        for (int i = 0; i < pre; ++i) load(i, i);  // (weights and scales only: nothing here waits for the previous
-                                                   // kernel)
+        for (int i = 0; i < pre; ++i) load(c0 + i, i);  // (weights and scales only: nothing here waits for the
+                                                        // previous kernel)
         if (lane == 0) grid_dep_launch();
         for (int i = pre; i < total; ++i) {
             const int s = i % ns;
             ok = mbar_wait(&empty[s], ((i / ns) - 1) & 1);
             if (!ok) break;
-            load(i, s);
+            load(c0 + i, s);
         }
         __syncwarp();
-        return;
-    }
+        if (ks == 1) return;
+        grid_dep_wait();  // (before the cluster's output stores)
+    } else {
 
     // ------------------------------ consumer warps ------------------------------
     grid_dep_wait();  // x may be the previous kernel's output (and before any output store of this kernel)
@@ -294,7 +301,7 @@ __global__ void __launch_bounds__(QQ_THREADS, QqFoot<BITS, NMAT>::kMinBlocks)
     // past K are skipped whole.
     const uint8_t* xg = reinterpret_cast<const uint8_t*>(a.x);
     auto fetch_x = [&](int i, uint4 (&u)[MT][2]) {
-        const int gi = 8 * i + warp;
+        const int gi = 8 * (c0 + i) + warp;
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
             const int tok = 8 * mt + g;
@@ -321,7 +328,7 @@ __global__ void __launch_bounds__(QQ_THREADS, QqFoot<BITS, NMAT>::kMinBlocks)
             if (i + 2 < total) fetch_x(i + 2, xnn);  // two stages ahead of its use
         }
         if (ok) ok = mbar_wait(&full[s], (i / ns) & 1);
-        if (ok && 8 * i + warp < a.kg) {
+        if (ok && 8 * (c0 + i) + warp < a.kg) {
             const uint32_t st = smem_base + s * S::STAGE_BYTES;
             // x fragments of group w permuted to the code order of a k16 step, and the group's x sums in the
             // accumulator layout (sx[mt][e] = sum(x) of token column 2t + (e & 1); rows are alike, entries 2 and 3 go
@@ -471,17 +478,56 @@ __global__ void __launch_bounds__(QQ_THREADS, QqFoot<BITS, NMAT>::kMinBlocks)
         return ((p[0] + p[1]) + (p[2] + p[3])) + ((p[4] + p[5]) + (p[6] + p[7]));
     };
     const int R = nu * 16;
-    for (int idx = threadIdx.x; idx < R * mv; idx += 32 * QQ_CW) {
-        const int tok = idx / R, row = idx - tok * R;
+    if (ks == 1) {
+        for (int idx = threadIdx.x; idx < R * mv; idx += 32 * QQ_CW) {
+            const int tok = idx / R, row = idx - tok * R;
+            const int n = row0 + row;
+            if (n >= a.N) continue;
+            float v;
+            if constexpr (NMAT == 2)
+                v = qq_swiglu<T>(sum_warps(tok, row), sum_warps(tok, FR * 16 + row));
+            else
+                v = sum_warps(tok, row);
+            if (ok) qq_store(a, tok, n, v, kBF16);
+        }
+        return;
+    }
+    // K slices: this CTA's sums [matrix][token][FR * 16 rows] after the warps' table, for the cluster to add
+    float* part = red + S::RED_BYTES / 4;
+    for (int idx = threadIdx.x; idx < NMAT * mv * R; idx += 32 * QQ_CW) {
+        const int m = idx / (mv * R), rem = idx - m * (mv * R), tok = rem / R, row = rem - tok * R;
+        part[(m * S::MTOK + tok) * (FR * 16) + row] = ok ? sum_warps(tok, m * FR * 16 + row) : 0.0f;
+    }
+    }  // (consumer warps)
+
+    // ------------------ the K slices added over the cluster (distributed shared memory) ------------------
+    cluster_sync();
+    const uint32_t part_local = smem_u32(smem) + S::RED_BYTES;
+    uint32_t peer[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) peer[q] = map_peer(part_local, q < ks ? q : 0);
+    const int R = nu * 16;
+    for (int idx = krank * QQ_THREADS + int(threadIdx.x); idx < R * mv; idx += ks * QQ_THREADS) {
+        const int tok = idx / R, row = idx - tok * R;  // consecutive threads: consecutive output columns
         const int n = row0 + row;
         if (n >= a.N) continue;
-        float v;
-        if constexpr (NMAT == 2)
-            v = qq_swiglu<T>(sum_warps(tok, row), sum_warps(tok, FR * 16 + row));
-        else
-            v = sum_warps(tok, row);
-        if (ok) qq_store(a, tok, n, v, kBF16);
+        // every slice's partial requested before any is added (one round of remote latency); slices in rank order
+        float v[8], u[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            v[q] = q < ks ? ld_dsmem_f(peer[q] + 4 * (tok * (FR * 16) + row)) : 0.0f;
+            if constexpr (NMAT == 2) u[q] = q < ks ? ld_dsmem_f(peer[q] + 4 * ((S::MTOK + tok) * (FR * 16) + row)) : 0.0f;
+        }
+        float g0 = 0.0f, u0s = 0.0f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            g0 += v[q];
+            if constexpr (NMAT == 2) u0s += u[q];
+        }
+        if constexpr (NMAT == 2) g0 = qq_swiglu<T>(g0, u0s);
+        if (ok) qq_store(a, tok, n, g0, kBF16);
     }
+    cluster_sync();  // the slices keep their shared memory until every CTA of the cluster has read it
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -504,7 +550,8 @@ static int qmvq_launch_t(const uint32_t* const* w, QqArgs a, int ns_req, int nct
     if (ns < 1) return LQ_E_SHAPE;
     a.ns = ns;
     size_t ring = size_t(ns) * S::STAGE_BYTES;
-    if (ring < size_t(S::RED_BYTES)) ring = S::RED_BYTES;
+    const size_t red_need = size_t(S::RED_BYTES) + (a.ks > 1 ? size_t(S::PART_BYTES) : 0);
+    if (ring < red_need) ring = red_need;
     const size_t smem = ring + fixed;
     if (smem > di.smem_optin) return LQ_E_SHAPE;
 
@@ -531,15 +578,23 @@ static int qmvq_launch_t(const uint32_t* const* w, QqArgs a, int ns_req, int nct
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return LQ_E_CUDA;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(nctas, 1, 1);
+    cfg.gridDim = dim3(nctas, a.ks, 1);
     cfg.blockDim = dim3(QQ_THREADS, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    int na = 1;
+    if (a.ks > 1) {  // the K slices of a unit range form one cluster along y
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = 1;
+        attr[1].val.clusterDim.y = a.ks;
+        attr[1].val.clusterDim.z = 1;
+        na = 2;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = na;
     e = cudaLaunchKernelEx(&cfg, kern, tw[0], tw[1], tw[2], tw[3], a);
     return e == cudaSuccess ? LQ_OK : LQ_E_CUDA;
 }
@@ -585,18 +640,40 @@ bool qmvq_shape_ok(int M, int K, int bits) {
 }
 
 // The grid and fragment count of a call: CTAs of at most fr units each (0 = spread over every SM); every CTA then
-// holds FR or FR - 1 units with FR = ceil(units / nctas), the two weight-box heights the kernel is given.
-static int qmvq_grid(int units, int fr_req, int max_fr, int* nctas) {
+// holds FR or FR - 1 units with FR = ceil(units / nctas), the two weight-box heights the kernel is given. With
+// ks K slices (clusters of ks CTAs along y) the unit CTAs are fewer: about sms / ks of them.
+static int qmvq_grid(int units, int fr_req, int max_fr, int ks, int* nctas) {
     const int sms = device_info().sm_count;
+    const int slots = sms / ks > 0 ? sms / ks : 1;
     int fr = fr_req;
     if (fr == 0) {
-        fr = (units + sms - 1) / sms;
+        fr = (units + slots - 1) / slots;
         if (fr > max_fr) fr = max_fr;
     }
     int n = (units + fr - 1) / fr;
-    if (fr_req == 0 && n < sms) n = units < sms ? units : sms;
+    if (fr_req == 0 && n < slots) n = units < slots ? units : slots;
     *nctas = n;
     return (units + n - 1) / n;
+}
+
+// K slices for the library's choice: the fewest stage-fragments a CTA (units a CTA x stages a slice) with the grid
+// within one CTA an SM (clusters of at most 8); a tie keeps fewer slices. Long-K matrices with few rows gain: the
+// 2560 x 9728 down projection goes from 2 units x 19 stages a CTA to 6 x 4.
+static int qmvq_choose_ks(int units, int nchunk, int max_fr) {
+    const int sms = device_info().sm_count;
+    int best_ks = 1;
+    long best = -1;
+    for (int ks = 1; ks <= 8 && ks <= nchunk; ++ks) {
+        const int slots = sms / ks;
+        const int fr = (units + slots - 1) / slots;
+        if (fr > max_fr) continue;
+        const long work = long(fr) * ((nchunk + ks - 1) / ks);
+        if (best < 0 || work < best) {
+            best = work;
+            best_ks = ks;
+        }
+    }
+    return best_ks;
 }
 
 static int qmvq_common(int nmat, const void* x, const uint32_t* const* w, const void* const* s, const void* const* b,
@@ -623,11 +700,14 @@ static int qmvq_common(int nmat, const void* x, const uint32_t* const* w, const 
     a.nseg_out = nout;
     const int fr_req = p ? p[0] : 0;
     const int ns = p ? p[1] : 0;
+    const int ks_req = p ? p[2] : 0;
     const int sxm = p ? p[3] : 0;
     const int max_fr = (bits == 4 && nmat == 1) ? QqFoot<4, 1>::kMaxFr : QqFoot<8, 1>::kMaxFr;
-    if (fr_req < 0 || fr_req > max_fr || ns < 0 || (p && p[2] != 0) || sxm < 0 || sxm > 2) return LQ_E_ARG;
+    if (fr_req < 0 || fr_req > max_fr || ns < 0 || ks_req < 0 || ks_req > 8 || sxm < 0 || sxm > 2) return LQ_E_ARG;
+    a.ks = ks_req > 0 ? ks_req : (fr_req > 0 ? 1 : qmvq_choose_ks(a.units, a.nchunk, max_fr));
+    if (a.ks > a.nchunk) a.ks = a.nchunk;
     int nctas = 0;
-    const int FR = qmvq_grid(a.units, fr_req, max_fr, &nctas);
+    const int FR = qmvq_grid(a.units, fr_req, max_fr, a.ks, &nctas);
     if (FR > max_fr) return LQ_E_SHAPE;
     const bool bf16 = dtype == LQ_BF16, sxa = sxm == 2;
     if (nmat == 1)
@@ -637,8 +717,8 @@ static int qmvq_common(int nmat, const void* x, const uint32_t* const* w, const 
                 : qmvq_dispatch<__half, 2>(bits, M, sxa, FR, w, a, ns, nctas, st);
 }
 
-// p = {FR (max units a CTA, 0 = spread over every SM), NS (stages, 0 = choose), 0, SX (group x sums: 0 = choose,
-// 1 = by an all-ones MMA, 2 = by fp32 adds and shuffles, 4-bit only)}.
+// p = {FR (max units a CTA, 0 = spread over every SM), NS (stages, 0 = choose), KS (K slices reduced over a cluster,
+// 1-8, 0 = choose), SX (group x sums: 0 = choose, 1 = by an all-ones MMA, 2 = by fp32 adds and shuffles, 4-bit only)}.
 int qmvq_run(const void* x, const uint32_t* w, const void* s, const void* b, int nout, void* const* outs,
              const int* seg_end, const int* ldo, int M, int N, int K, int bits, int dtype, const int* p,
              cudaStream_t st) {

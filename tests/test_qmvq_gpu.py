@@ -68,7 +68,10 @@ def test_qmvq_ragged(cuda, M, N, K, dtype, sx):
                                     ("qmvq", 4, 0, 0, 0), ("qmvq", 3, 1, 0, 0), ("qmvq", 2, 2, 0, 0), ("qmvq", 4, 3, 0, 0),
                                     # group x sums by the all-ones MMA or by adds
                                     ("qmvq", 0, 0, 0, 1), ("qmvq", 0, 0, 0, 2), ("qmvq", 3, 2, 0, 2),
-                                    ("qmvq", 1, 0, 0, 1), ("qmvq", 4, 0, 0, 2)])
+                                    ("qmvq", 1, 0, 0, 1), ("qmvq", 4, 0, 0, 2),
+                                    # K slices added over a cluster (2-5 CTAs along y)
+                                    ("qmvq", 0, 0, 2, 0), ("qmvq", 0, 0, 3, 1), ("qmvq", 2, 0, 4, 0),
+                                    ("qmvq", 4, 2, 5, 2)])
 def test_qmvq_every_tiling(cuda, choice):
     y, ref = _run(cuda, 16, 1552, 2560, "bfloat16", seed=21, choice=choice)
     assert rel_err(y, ref) <= TOL_REL
@@ -154,4 +157,45 @@ def test_qmvq_glu(cuda, bits, M, I, K, dtype):
     assert kernels.device_status() == 0
     # four activation-dtype roundings before act * u: the reference bounds its own expert SwiGLU output by 2^-6 max
     # (tests/test_flint.py:80-111)
+    assert rel_err(h.float().cpu().numpy(), href) <= 2.0 ** -6
+
+
+@pytest.mark.parametrize("bits,M,N,K,ks", [
+    (8, 1, 2560, 9728, 0),     # config 3's down projection: the library's choice splits K (5 slices)
+    (8, 16, 2560, 9728, 8),
+    (4, 3, 2560, 9728, 0),
+    (4, 9, 1000, 4608, 3),     # a partial fragment, uneven slices
+    (8, 2, 64, 768, 3),        # one stage a slice
+])
+def test_qmvq_k_slices(cuda, bits, M, N, K, ks):
+    """K split over a thread-block cluster, the slices' sums added in rank order through distributed shared memory."""
+    import torch
+    from locals_b200 import kernels
+
+    rng = np.random.default_rng(bits + M + N + K + ks)
+    wq, s, b = qweights(rng, N, K, bits, "bfloat16")
+    x = act(rng, M, K, "bfloat16")
+    ref = O.round_to(O.qmm(x, wq, s, b, 64, bits), "bfloat16")
+    tw, ts, tb = to_torch(wq, s, b, "bfloat16", cuda)
+    y = kernels.quantized_matmul(x_torch(x, "bfloat16", cuda), tw, ts, tb, bits=bits, choice=("qmvq", 0, 0, ks, 0))
+    torch.cuda.synchronize()
+    assert kernels.device_status() == 0
+    assert rel_err(y.float().cpu().numpy(), ref) <= TOL_REL
+
+
+def test_qmvq_glu_k_slices(cuda):
+    import torch
+    from locals_b200 import kernels
+
+    rng = np.random.default_rng(31)
+    M, I, K = 4, 1024, 4096
+    g = qweights(rng, I, K, 8, "bfloat16")
+    u = qweights(rng, I, K, 8, "bfloat16")
+    x = act(rng, M, K, "bfloat16")
+    href = O.swiglu(O.round_to(O.qmm(x, *g, 64, 8), "bfloat16"), O.round_to(O.qmm(x, *u, 64, 8), "bfloat16"),
+                    "bfloat16")
+    tg, tu = to_torch(*g, "bfloat16", cuda), to_torch(*u, "bfloat16", cuda)
+    h = kernels.qmm_glu(x_torch(x, "bfloat16", cuda), tg, tu, bits=8, choice=("qmvq", 0, 0, 4, 0))
+    torch.cuda.synchronize()
+    assert kernels.device_status() == 0
     assert rel_err(h.float().cpu().numpy(), href) <= 2.0 ** -6
