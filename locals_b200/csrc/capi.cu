@@ -57,6 +57,11 @@ int qmvq_run(const void* x, const uint32_t* w, const void* s, const void* b, int
 int qmvq_glu_run(const void* x, const uint32_t* w_gate, const void* s_gate, const void* b_gate, const uint32_t* w_up,
                  const void* s_up, const void* b_up, void* h, int M, int I, int K, int bits, int dtype, const int* p,
                  cudaStream_t st);
+bool qmvqg_shape_ok(int max_rows, int N, int K, int bits);
+int qmvqg_run(const void* x, const int32_t* gather, int gather_k, const int32_t* starts, const int32_t* experts,
+              const int32_t* nseg, int P, int max_rows, int glu, const uint32_t* w0, const void* s0, const void* b0,
+              const uint32_t* w1, const void* s1, const void* b1, void* out, int E, int N, int K, int bits, int dtype,
+              cudaStream_t st);
 bool qmvg_moe_ok(int mode, int k, int rows_e, int K, int sms);
 int qmvg_moe_run(int mode, const void* x, const int32_t* experts, const int32_t* pos, const float* wts,
                  const uint32_t* w0, const void* s0, const void* b0, const uint32_t* w1, const void* s1, const void* b1,
@@ -386,6 +391,13 @@ int lq_moe_experts(const void* xs, const int32_t* starts, const int32_t* experts
         qmvg_moe_ok(1, gather_k, N, K, device_info().sm_count)) {
         rc = qmvg_moe_run(1, xs, experts, nullptr, nullptr, w0, s0, b0, w1, s1, b1, out, gather_k, E, N, K, dtype,
                           reinterpret_cast<cudaStream_t>(stream));
+        if (rc != LQ_E_SHAPE) return finish(rc);
+    }
+    // up to 16 rows a segment (decode batches): the grouped folded kernel, every SM walking (segment, fragment
+    // chunk) items with one ring of weight stages running on across them
+    if (P < 1024 && qmvqg_shape_ok(max_rows, N, K, bits)) {
+        rc = qmvqg_run(xs, gather_order, gather_k, starts, experts, nseg, P, max_rows, glu, w0, s0, b0, w1, s1, b1,
+                       out, E, N, K, bits, dtype, reinterpret_cast<cudaStream_t>(stream));
         if (rc != LQ_E_SHAPE) return finish(rc);
     }
     // from 1024 routed rows (about 16 per expert at 64 experts) the expert GEMMs run on the tensor-core
