@@ -157,6 +157,22 @@ int lq_moe_down_combine(const void* h, const int32_t* experts, const int32_t* po
                         const uint32_t* w, const void* s, const void* b, void* y, int k, int E, int N, int K, int bits,
                         int group_size, int dtype, void* stream);
 
+/* ONE token's whole routed MoE layer in one launch (decode at batch 1): the router logits and top-k of lq_moe_route
+ * (bit-identical experts and weights), each slot's gate/up SwiGLU, its down projection and the weighted combine of
+ * lq_moe_down_combine, y (1, D) in dtype. Replaces, for one token, the chain router -> route_topk -> experts_up ->
+ * experts_down of the reference's FusedFlintMoe.__call__ (locals/moe.py:577-591) without its shared expert.
+ * x (1, D) dtype; router_w (E, D) f16/bf16; gate/up (E, I, D/8) packed 4-bit, down (E, D, I/8), scales and biases
+ * (E, rows, K/64) in dtype, group size 64, every pointer 16-byte aligned. inds (k) and weights (k) receive the routing when not NULL. workspace:
+ * lq_moe_decode_workspace(E, k, D, I) bytes, 16-byte aligned, zero-filled before its first use (the kernel leaves
+ * its counters at zero); one workspace serves launches in stream order, not concurrent launches. D % 128 == 0,
+ * I % 64 == 0, k <= 32, E <= 1024; LQ_E_SHAPE outside this (use the unfused calls then). */
+size_t lq_moe_decode_workspace(int E, int k, int D, int I);
+int lq_moe_decode(const void* x, const void* router_w, int router_dtype, int E, int k, int mode, const uint32_t* wg,
+                  const void* sg, const void* bg, const uint32_t* wu, const void* su, const void* bu,
+                  const uint32_t* wd, const void* sd, const void* bd, int D, int I, int bits, int group_size,
+                  int dtype, void* y, uint32_t* inds, float* weights, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
 /* y (T, D) = sum over slots r of weights[t, r] * ys[pos[t*k + r], :] in float32, slots in order, rounded
  * to dtype (locals/moe.py:339-348). pos == NULL reads row t*k + r. */
 int lq_moe_combine(const void* ys, const float* weights, const int32_t* pos, void* y, int T, int k, int D, int dtype,

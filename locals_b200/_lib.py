@@ -38,6 +38,9 @@ SIGNATURES = {
     "lq_moe_route": ([_vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp], _i),
     "lq_moe_combine": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp], _i),
     "lq_moe_down_combine": ([_vp, _vp, _vp, _vp, _u32p, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp], _i),
+    "lq_moe_decode_workspace": ([_i, _i, _i, _i], ctypes.c_size_t),
+    "lq_moe_decode": ([_vp, _vp, _i, _i, _i, _i, _u32p, _vp, _vp, _u32p, _vp, _vp, _u32p, _vp, _vp, _i, _i, _i, _i, _i,
+                       _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp], _i),
     "lq_add_rms_norm": ([_vp, _vp, _vp, _vp, _vp, _i, _i, ctypes.c_float, _i, _vp], _i),
     "lq_moe_combine_norm": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, ctypes.c_float, _i, _vp], _i),
     "lq_scatter_rows": ([_vp, _vp, _i, _i, _vp, _i, _i, _vp], _i),

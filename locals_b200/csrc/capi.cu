@@ -66,6 +66,11 @@ bool qmvg_moe_ok(int mode, int k, int rows_e, int K, int sms);
 int qmvg_moe_run(int mode, const void* x, const int32_t* experts, const int32_t* pos, const float* wts,
                  const uint32_t* w0, const void* s0, const void* b0, const uint32_t* w1, const void* s1, const void* b1,
                  void* out, int k, int E, int rows_e, int K, int dtype, cudaStream_t st);
+bool moe_decode_ok(int E, int k, int D, int I);
+size_t moe_decode_workspace_bytes(int E, int k, int D, int I);
+int moe_decode_run(const void* x, int x_dt, const void* rw, int rw_dt, int E, int k, int mode, const uint32_t* const* w,
+                   const void* const* s, const void* const* b, int D, int I, void* y, uint32_t* inds, float* wts,
+                   void* work, size_t work_bytes, cudaStream_t st);
 bool kv_attend_shape_ok(int B, int H, int KVH, int n, int cap, int head_dim);
 size_t kv_attend_workspace_bytes(int B, int H, int KVH, int n, int sms);
 int kv_attend_run(const void* q, const uint32_t* kq, const void* ks, const void* kb, const uint32_t* vq,
@@ -434,6 +439,37 @@ int lq_moe_down_combine(const void* h, const int32_t* experts, const int32_t* po
     if (!aligned(y, 2) || !aligned(weights, 4) || !aligned(experts, 4) || !aligned(pos, 4)) return LQ_E_ALIGN;
     return finish(qmvg_moe_run(2, h, experts, pos, weights, w, s, b, nullptr, nullptr, nullptr, y, k, E, N, K, dtype,
                                reinterpret_cast<cudaStream_t>(stream)));
+}
+
+size_t lq_moe_decode_workspace(int E, int k, int D, int I) {
+    if (check_device() != LQ_OK) return 0;
+    return moe_decode_workspace_bytes(E, k, D, I);
+}
+
+int lq_moe_decode(const void* x, const void* router_w, int router_dtype, int E, int k, int mode, const uint32_t* wg,
+                  const void* sg, const void* bg, const uint32_t* wu, const void* su, const void* bu,
+                  const uint32_t* wd, const void* sd, const void* bd, int D, int I, int bits, int group_size,
+                  int dtype, void* y, uint32_t* inds, float* weights, void* workspace, size_t workspace_bytes,
+                  void* stream) {
+    int rc = check_common(x, wg, sg, bg, 1, I, D, bits, group_size, dtype);
+    if (rc) return rc;
+    rc = check_common(x, wu, su, bu, 1, I, D, bits, group_size, dtype);
+    if (rc) return rc;
+    rc = check_common(x, wd, sd, bd, 1, D, I, bits, group_size, dtype);
+    if (rc) return rc;
+    if (!router_w || !y || !workspace || (inds == nullptr) != (weights == nullptr)) return LQ_E_ARG;
+    if (!is16(router_dtype)) return LQ_E_UNSUPPORTED;
+    if (mode != 0 && mode != 1) return LQ_E_ARG;
+    if (bits != 4 || !moe_decode_ok(E, k, D, I)) return LQ_E_SHAPE;
+    if (!aligned(router_w, 16) || !aligned(y, 2) || !aligned(inds, 4) || !aligned(weights, 4) ||
+        !aligned(workspace, 16) || !aligned(sg, 16) || !aligned(bg, 16) || !aligned(su, 16) || !aligned(bu, 16) ||
+        !aligned(sd, 16) || !aligned(bd, 16))
+        return LQ_E_ALIGN;
+    const uint32_t* w[3] = {wg, wu, wd};
+    const void* s[3] = {sg, su, sd};
+    const void* b[3] = {bg, bu, bd};
+    return finish(moe_decode_run(x, dtype, router_w, router_dtype, E, k, mode, w, s, b, D, I, y, inds, weights,
+                                 workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream)));
 }
 
 int lq_add_rms_norm(const void* x, const void* r, const void* w, void* h, void* n, int rows, int D, float eps,

@@ -19,6 +19,7 @@
 #include "lq_host.h"
 #include "lq_ptx.cuh"
 #include "lq_status.cuh"
+#include "moe_route.cuh"
 
 namespace lq {
 
@@ -39,22 +40,6 @@ static int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem
     return cuda_status(cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...));
 }
 
-__device__ __forceinline__ void unpack8(uint4 u, int dt, float* f) {
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        if (dt == LQ_BF16) {
-            f[2 * i] = __uint_as_float(w[i] << 16);
-            f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-        } else {
-            const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
-            const float2 v = __half22float2(h);
-            f[2 * i] = v.x;
-            f[2 * i + 1] = v.y;
-        }
-    }
-}
-
 // grid: T * ceil(E / 4) blocks of 128 threads (4 warps = 4 experts of one token)
 __global__ void router_logits_kernel(const void* x, int x_dt, const void* w, int w_dt, float* logits, int T, int E,
                                      int D) {
@@ -65,62 +50,9 @@ __global__ void router_logits_kernel(const void* x, int x_dt, const void* w, int
     const int t = blockIdx.x / eb;
     const int e = (blockIdx.x % eb) * 4 + warp;
     if (t >= T || e >= E) return;
-    const uint4* xr = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + size_t(t) * D);
-    const uint4* wr = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(w) + size_t(e) * D);
-    float acc = 0.0f;
-    for (int i = lane; i < D / 8; i += 32) {
-        float xf[8], wf[8];
-        unpack8(xr[i], x_dt, xf);
-        unpack8(wr[i], w_dt, wf);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc = fmaf(xf[j], wf[j], acc);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    const float acc = router_dot(reinterpret_cast<const uint16_t*>(x) + size_t(t) * D, x_dt,
+                                 reinterpret_cast<const uint16_t*>(w) + size_t(e) * D, w_dt, D, lane);
     if (lane == 0) logits[size_t(t) * E + e] = acc;
-}
-
-constexpr int TOPK_MAX_PER_LANE = 32;  // E <= 1024
-
-// k rounds of a warp argmax over E scores held `per` per lane (expert lane + 32 j), ties to the lower
-// index, then renormalisation; lane 0 writes k indices and weights. NaN scores rank below every number.
-__device__ __forceinline__ void topk_select(float* sc, int per, int E, int k, int lane, uint32_t* inds,
-                                            float* weights) {
-    for (int j = 0; j < per; ++j)
-        if (isnan(sc[j])) sc[j] = -2.0f;
-    float picked_sum = 0.0f;
-    float picked[32];
-    uint32_t which[32];
-    for (int r = 0; r < k; ++r) {
-        float best = -3.0f;
-        int best_e = E;
-        for (int j = 0; j < per; ++j) {
-            const int e = lane + 32 * j;
-            if (e < E && sc[j] > best) {  // strict: the lower index of this lane wins ties
-                best = sc[j];
-                best_e = e;
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-            const int oe = __shfl_xor_sync(0xffffffffu, best_e, o);
-            if (ob > best || (ob == best && oe < best_e)) {
-                best = ob;
-                best_e = oe;
-            }
-        }
-        if (best_e < E && (best_e & 31) == lane) sc[best_e >> 5] = -3.0f;
-        picked[r] = best < -1.5f ? 0.0f : best;
-        which[r] = uint32_t(best_e < E ? best_e : E - 1);
-        picked_sum += picked[r];
-    }
-    if (lane == 0) {
-        for (int r = 0; r < k; ++r) {
-            inds[r] = which[r];
-            weights[r] = picked[r] / picked_sum;
-        }
-    }
 }
 
 // one warp per token; 4 tokens per block
@@ -132,37 +64,7 @@ __global__ void route_topk_kernel(const float* logits, int T, int E, int k, int 
     const int t = blockIdx.x * 4 + warp;
     if (t >= T) return;
     const float* l = logits + size_t(t) * E;
-    const int per = (E + 31) / 32;
-    float sc[TOPK_MAX_PER_LANE];
-    if (mode == 0) {
-        float mx = -INFINITY;
-        for (int j = 0; j < per; ++j) {
-            const int e = lane + 32 * j;
-            sc[j] = e < E ? l[e] : -INFINITY;
-            mx = fmaxf(mx, sc[j]);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float tot = 0.0f;
-        for (int j = 0; j < per; ++j) {
-            const int e = lane + 32 * j;
-            sc[j] = e < E ? expf(sc[j] - mx) : 0.0f;
-            tot += sc[j];
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-        for (int j = 0; j < per; ++j) {
-            const int e = lane + 32 * j;
-            sc[j] = e < E ? sc[j] / tot : -1.0f;
-        }
-    } else {
-        for (int j = 0; j < per; ++j) {
-            const int e = lane + 32 * j;
-            const float v = e < E ? 1.0f / (1.0f + expf(-l[e])) : -1.0f;
-            sc[j] = e < E ? (isnan(v) ? 0.0f : v) : -1.0f;
-        }
-    }
-    topk_select(sc, per, E, k, lane, inds + size_t(t) * k, weights + size_t(t) * k);
+    score_and_select([&](int e) { return l[e]; }, E, k, mode, lane, inds + size_t(t) * k, weights + size_t(t) * k);
 }
 
 // One CTA of 1024 threads. order/starts/experts/nseg as lq_moe_group; pos = inverse of order (optional).
@@ -284,8 +186,9 @@ __global__ void combine_kernel(const uint16_t* ys, const float* w, const int32_t
     }
 }
 
-// Router logits and top-k, the experts split over a cluster of RC_CL CTAs and the tokens in tiles of RC_TT (grid
-// (ceil(T / RC_TT), RC_CL), cluster (1, RC_CL, 1), 256 threads). Each CTA stages its E / RC_CL experts' router rows in
+// Router logits and top-k, the experts split over a cluster of RC_CL CTAs and the tokens in tiles of TT (grid
+// (ceil(T / TT), RC_CL), cluster (1, RC_CL, 1), 256 threads; TT = ceil(T / 16) up to RC_TT, so up to 16 tokens run
+// one token a cluster). Each CTA stages its E / RC_CL experts' router rows in
 // shared memory BEFORE waiting for the previous kernel (they do not depend on it; at config 4 a CTA's 8 rows are
 // 32 KB, so the weights are read by eight SMs at once instead of one), computes the float32 dot products of its
 // experts with the tile's tokens (16-byte loads, one warp a (token, expert)), and keeps the logits in shared memory.
@@ -293,57 +196,20 @@ __global__ void combine_kernel(const uint16_t* ys, const float* w, const int32_t
 // and picks the top k exactly as route_topk_kernel does. logits_out may be null.
 constexpr int ROUTE_MAX_E = 1024;
 constexpr int RC_CL = 8;
-constexpr int RC_TT = 8;
+constexpr int RC_TT = 8;  // the largest token tile
 constexpr size_t RC_STAGE_MAX = 64 * 1024;
 
-// softmax (mode 0) or sigmoid (mode 1, NaN -> 0) of the E logits fetched by get(e), then the top k
-template <typename Get>
-__device__ __forceinline__ void score_and_select(Get get, int E, int k, int mode, int lane, uint32_t* inds,
-                                                 float* weights) {
-    const int per = (E + 31) / 32;
-    float sc[TOPK_MAX_PER_LANE];
-    if (mode == 0) {
-        float mx = -INFINITY;
-        for (int j = 0; j < per; ++j) {
-            const int e = lane + 32 * j;
-            sc[j] = e < E ? get(e) : -INFINITY;
-            mx = fmaxf(mx, sc[j]);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float tot = 0.0f;
-        for (int j = 0; j < per; ++j) {
-            const int e = lane + 32 * j;
-            sc[j] = e < E ? expf(sc[j] - mx) : 0.0f;
-            tot += sc[j];
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-        for (int j = 0; j < per; ++j) {
-            const int e = lane + 32 * j;
-            sc[j] = e < E ? sc[j] / tot : -1.0f;
-        }
-    } else {
-        for (int j = 0; j < per; ++j) {
-            const int e = lane + 32 * j;
-            const float v = e < E ? 1.0f / (1.0f + expf(-get(e))) : -1.0f;
-            sc[j] = e < E ? (isnan(v) ? 0.0f : v) : -1.0f;
-        }
-    }
-    topk_select(sc, per, E, k, lane, inds, weights);
-}
-
 __global__ void __launch_bounds__(256) router_topk_kernel(const void* x, int x_dt, const void* w, int w_dt, int T,
-                                                          int E, int D, int k, int mode, int staged, uint32_t* inds,
-                                                          float* weights, float* logits_out) {
+                                                          int E, int D, int k, int mode, int staged, int TT,
+                                                          uint32_t* inds, float* weights, float* logits_out) {
     extern __shared__ __align__(16) uint8_t rsm[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rank = int(cluster_ctarank());
     const int EC = (E + RC_CL - 1) / RC_CL;
     const int e0 = rank * EC;
     const int ne = E - e0 < EC ? (E - e0 > 0 ? E - e0 : 0) : EC;
-    float* lg = reinterpret_cast<float*>(rsm);  // [RC_TT][EC]
-    const size_t lg_bytes = (size_t(RC_TT) * EC * 4 + 15) / 16 * 16;
+    float* lg = reinterpret_cast<float*>(rsm);  // [TT][EC]
+    const size_t lg_bytes = (size_t(TT) * EC * 4 + 15) / 16 * 16;
     const uint16_t* wrows = reinterpret_cast<const uint16_t*>(w) + size_t(e0) * D;
     uint16_t* wsm = reinterpret_cast<uint16_t*>(rsm + lg_bytes);
     const size_t wbytes = (staged & 1) ? (size_t(EC) * D * 2 + 15) / 16 * 16 : 0;
@@ -355,8 +221,8 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const void* x, int x_d
     }
     grid_dep_wait();
     grid_dep_launch();
-    const int t0 = blockIdx.x * RC_TT;
-    const int tt = T - t0 < RC_TT ? T - t0 : RC_TT;
+    const int t0 = blockIdx.x * TT;
+    const int tt = T - t0 < TT ? T - t0 : TT;
     const uint16_t* xtile = reinterpret_cast<const uint16_t*>(x) + size_t(t0) * D;
     if (staged & 2) {  // the tile's tokens, every 16-byte load in flight at once
         const int n16 = tt * D / 8;
@@ -369,19 +235,7 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const void* x, int x_d
     const uint16_t* xsrc = (staged & 2) ? xsm : xtile;
     for (int it = warp; it < tt * ne; it += 8) {
         const int tl = it / ne, el = it - tl * ne;
-        const uint4* xr = reinterpret_cast<const uint4*>(xsrc + size_t(tl) * D);
-        const uint4* wr = reinterpret_cast<const uint4*>(wsrc + size_t(el) * D);
-        float acc = 0.0f;
-#pragma unroll 4
-        for (int i = lane; i < D / 8; i += 32) {
-            float xf[8], wf[8];
-            unpack8(xr[i], x_dt, xf);
-            unpack8(wr[i], w_dt, wf);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) acc = fmaf(xf[j], wf[j], acc);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        const float acc = router_dot(xsrc + size_t(tl) * D, x_dt, wsrc + size_t(el) * D, w_dt, D, lane);
         if (lane == 0) {
             lg[tl * EC + el] = acc;
             if (logits_out) logits_out[size_t(t0 + tl) * E + e0 + el] = acc;
@@ -403,9 +257,10 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const void* x, int x_d
 int router_topk_run(const void* x, int x_dt, const void* w, int w_dt, int T, int E, int D, int k, int mode,
                     uint32_t* inds, float* weights, float* logits, cudaStream_t st) {
     const int EC = (E + RC_CL - 1) / RC_CL;
-    const size_t lg_bytes = (size_t(RC_TT) * EC * 4 + 15) / 16 * 16;
+    const int TT = T <= 16 ? 1 : ((T + 15) / 16 < RC_TT ? (T + 15) / 16 : RC_TT);
+    const size_t lg_bytes = (size_t(TT) * EC * 4 + 15) / 16 * 16;
     const size_t wbytes = (size_t(EC) * D * 2 + 15) / 16 * 16;
-    const size_t xbytes = size_t(RC_TT) * D * 2;
+    const size_t xbytes = size_t(TT) * D * 2;
     // bit 0: router rows staged in shared memory; bit 1: the tile's tokens too (x is 16-byte aligned, D % 8 == 0)
     const int staged = ((wbytes <= RC_STAGE_MAX && (reinterpret_cast<uintptr_t>(w) % 16) == 0) ? 1 : 0) |
                        (xbytes <= RC_STAGE_MAX ? 2 : 0);
@@ -416,7 +271,7 @@ int router_topk_run(const void* x, int x_dt, const void* w, int w_dt, int T, int
         if (e != cudaSuccess) return LQ_E_CUDA;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((T + RC_TT - 1) / RC_TT, RC_CL, 1);
+    cfg.gridDim = dim3((T + TT - 1) / TT, RC_CL, 1);
     cfg.blockDim = dim3(256, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
@@ -429,8 +284,8 @@ int router_topk_run(const void* x, int x_dt, const void* w, int w_dt, int T, int
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cuda_status(cudaLaunchKernelEx(&cfg, router_topk_kernel, x, x_dt, w, w_dt, T, E, D, k, mode, staged, inds,
-                                          weights, logits));
+    return cuda_status(cudaLaunchKernelEx(&cfg, router_topk_kernel, x, x_dt, w, w_dt, T, E, D, k, mode, staged, TT,
+                                          inds, weights, logits));
 }
 
 int router_logits_run(const void* x, int x_dt, const void* w, int w_dt, float* logits, int T, int E, int D,

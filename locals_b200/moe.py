@@ -211,13 +211,62 @@ def switch_glu_grouped(x: torch.Tensor, inds: torch.Tensor, gate, up, down, bits
     return experts(h, grouping, [down], D, max_rows=M, bits=bits, group_size=group_size)
 
 
+_DECODE_WORK: dict = {}
+
+
+def decode_workspace(E: int, k: int, D: int, I: int, device) -> Optional[torch.Tensor]:
+    """The zero-filled workspace of lq_moe_decode for a shape (one per shape and device; launches in stream order may
+    share it -- the kernel leaves it zeroed), or None when the shape is outside the fused kernel."""
+    key = (E, k, D, I, str(device))
+    w = _DECODE_WORK.get(key)
+    if w is None:
+        n = int(_lib.lib().lq_moe_decode_workspace(E, k, D, I))
+        if n == 0:
+            return None
+        w = torch.zeros(n, dtype=torch.uint8, device=device)
+        _DECODE_WORK[key] = w
+    return w
+
+
+def decode(x: torch.Tensor, router_w: torch.Tensor, gate, up, down, k: int, mode: int = SOFTMAX, bits: int = 4,
+           group_size: int = 64, inds: Optional[torch.Tensor] = None, weights: Optional[torch.Tensor] = None,
+           workspace: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+    """One token's routed MoE layer in one kernel (lq_moe_decode): y (1, D), or None when the shape is outside the
+    fused kernel (the caller then runs route + experts + down_combine). inds (1, k) int32 and weights (1, k) float32,
+    when given, receive the routing."""
+    x2 = x.reshape(-1, x.shape[-1]).contiguous()
+    if x2.shape[0] != 1 or bits != 4 or group_size != 64:
+        return None
+    _check_cuda(x2, router_w)
+    D = x2.shape[1]
+    E = router_w.shape[0]
+    I = gate[0].shape[1]
+    work = workspace if workspace is not None else decode_workspace(E, k, D, I, x2.device)
+    if work is None:
+        return None
+    y = torch.empty((1, D), dtype=x2.dtype, device=x2.device)
+    rc = _lib.lib().lq_moe_decode(x2.data_ptr(), router_w.data_ptr(), dtype_code(router_w.dtype), E, k, mode,
+                                  gate[0].data_ptr(), gate[1].data_ptr(), gate[2].data_ptr(), up[0].data_ptr(),
+                                  up[1].data_ptr(), up[2].data_ptr(), down[0].data_ptr(), down[1].data_ptr(),
+                                  down[2].data_ptr(), D, I, bits, group_size, dtype_code(x2.dtype), y.data_ptr(),
+                                  None if inds is None else inds.data_ptr(),
+                                  None if weights is None else weights.data_ptr(), work.data_ptr(), work.numel(),
+                                  _stream())
+    if rc == _lib.LQ_E_SHAPE:
+        return None
+    if rc != _lib.LQ_OK:
+        raise _lib.LQError("lq_moe_decode", rc)
+    return y
+
+
 class MoELayer:
     """Router + top-k experts + combine over stacked MLX-affine experts (softmax routing, top-k renormalised)."""
 
     def __init__(self, router_w: torch.Tensor, gate, up, down, top_k: int, mode: int = SOFTMAX, bits: int = 4,
-                 group_size: int = 64):
+                 group_size: int = 64, fused_decode: bool = True):
         self.router_w, self.gate, self.up, self.down = router_w, gate, up, down
         self.top_k, self.mode, self.bits, self.group_size = top_k, mode, bits, group_size
+        self.fused_decode = fused_decode  # one token: lq_moe_decode (else route + experts + down_combine)
         self.n_experts = gate[0].shape[0]
 
     def route(self, x: torch.Tensor):
@@ -226,6 +275,11 @@ class MoELayer:
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         D = x.shape[-1]
         x2 = x.reshape(-1, D).contiguous()
+        if x2.shape[0] == 1 and self.fused_decode:  # one token: the whole layer in one kernel
+            y = decode(x2, self.router_w, self.gate, self.up, self.down, self.top_k, self.mode, self.bits,
+                       self.group_size)
+            if y is not None:
+                return y.reshape(x.shape)
         inds, wts = self.route(x2)
         grouping = direct_grouping(inds) if x2.shape[0] <= DIRECT_MAX_TOKENS else group(inds, self.n_experts)
         if x2.shape[0] == 1:  # one token: the down projections and the combine in one kernel
