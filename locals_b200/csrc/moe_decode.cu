@@ -7,9 +7,9 @@
 // c = blockIdx.y of C, cluster rank t = blockIdx.x. At config 4 (E 64, k 4, D 2048, I 768, 4-bit) C = 4: 128 CTAs.
 //   * Routing, in every cluster: CTA t stages the router rows of experts [t EC, (t + 1) EC) (EC = ceil(E / CS))
 //     BEFORE waiting for the previous kernel (they do not depend on it), computes their float32 logits with the
-//     library's one router dot product (moe_route.cuh), and after a cluster barrier every CTA reads all E logits
-//     through distributed shared memory and runs the softmax / sigmoid top-k of lq_moe_route: every CTA knows the k
-//     experts and weights, bit-identical to lq_moe_route's. CTA (0, 0, 0) writes them out.
+//     library's one router dot product (moe_route.cuh) and stores them into every peer's shared memory; after a
+//     cluster barrier every CTA runs the softmax / sigmoid top-k of lq_moe_route on all E logits: every CTA knows
+//     the k experts and weights, bit-identical to lq_moe_route's. CTA (0, 0, 0) writes them out.
 //   * Weights: with e = inds[j], the CTA copies (cp.async, all in flight together) gate and up rows
 //     [c I/C + t R, + R) (R = I / (C CS)) and down rows [t D/CS, + D/CS) restricted to the K slice
 //     [c I/C, (c + 1) I/C) into shared memory -- about 83 KB a CTA at config 4, so the layer's whole weight stream
@@ -19,7 +19,7 @@
 //     MMA's k order is a permutation of the group's 64 positions, applied to x (fragments built once) and to the
 //     codes alike. The 16 warps split K and their partial sums are added in warp order; h = swiglu with the
 //     activation-dtype rounding points of locals/moe.py:284-289.
-//   * Down: the cluster's h slice (I/C values, R from each CTA) is read through distributed shared memory; warp w
+//   * Down: each CTA stores its R values of h into every peer's copy of the cluster's h slice (I/C values); warp w
 //     computes row tiles w, w + 16, ... of the CTA's D/CS rows over the whole K slice and stores float32 partial sums.
 //   * Combine: the last CTA to finish row block t (a per-block atomic counter: no CTA waits for another) adds each
 //     slot's C partials in slice order, rounds the slot's output to the activation dtype and sums w_j y_j in slot
@@ -68,7 +68,7 @@ struct MdLayout {
     int gs, ds;     // gate/up row stride (padded) and down row stride (the TMA box's dense rows), bytes
     int DR, KS, gq;  // down rows a CTA, the K slice, its 64-groups
     int RT;          // gate/up row tiles of 16
-    size_t o_bar, o_rw, o_x, o_xf, o_sx, o_lg, o_sel, o_gu, o_gusb, o_dw, o_dsb, o_red, o_hm, o_hs, o_hf, o_hsx,
+    size_t o_bar, o_rw, o_x, o_xf, o_sx, o_lg, o_sel, o_gu, o_gusb, o_dw, o_dsb, o_red, o_hs, o_hf, o_hsx,
         o_flag, total;
 };
 
@@ -103,8 +103,8 @@ __host__ __device__ inline MdLayout md_layout(int E, int k, int D, int I, int C,
     o += size_t(D / 64) * 128;
     L.o_sx = o;
     o += md_up16(size_t(D / 64) * 4);
-    L.o_lg = o;
-    o += md_up16(size_t(EC) * 4);
+    L.o_lg = o;  // every expert's logit (each CTA's own written into every peer)
+    o += md_up16(size_t(E) * 4);
     L.o_sel = o;
     o += md_up16(size_t(k) * 8);
     L.o_gu = o;  // the gate/up rows; the last CTA of a row block stages the slices' partial sums here
@@ -115,8 +115,6 @@ __host__ __device__ inline MdLayout md_layout(int E, int k, int D, int I, int C,
     o += size_t(2) * L.DR * (I / 64) * 2;
     L.o_red = o;
     o += size_t(MD_WARPS) * 2 * L.RT * 16 * 4;
-    L.o_hm = o;
-    o += md_up16(size_t(R) * 2);
     L.o_hs = o;
     o += md_up16(size_t(L.KS) * 2);
     L.o_hf = o;
@@ -164,16 +162,14 @@ __device__ __forceinline__ uint2 md_lds64(uint32_t addr) {
     return v;
 }
 
-__device__ __forceinline__ uint16_t md_ld_dsmem_u16(uint32_t addr) {
-    uint16_t v;
-    asm volatile("ld.shared::cluster.u16 %0, [%1];" : "=h"(v) : "r"(addr) : "memory");
-    return v;
+// stores into a cluster peer's shared memory (addr from mapa); ordered before the peer's reads by the next
+// cluster barrier (release / acquire)
+__device__ __forceinline__ void md_st_dsmem_f(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
-
-__device__ __forceinline__ void md_cluster_arrive() {
-    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+__device__ __forceinline__ void md_st_dsmem_u16(uint32_t addr, uint16_t v) {
+    asm volatile("st.shared::cluster.u16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
 }
-__device__ __forceinline__ void md_cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
 template <typename T>
 __device__ __forceinline__ void md_mma(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -271,6 +267,8 @@ __global__ void __launch_bounds__(MD_THREADS, 1)
         fence_barrier_init();
         prefetch_tmap(&tm_down);
     }
+    // every CTA of the cluster has started before any CTA stores into a peer's shared memory (waited on below)
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 
     // ---- routing: this CTA's router rows (independent of the previous kernel), then x and the logits ----
     const uint16_t* rrows = reinterpret_cast<const uint16_t*>(a.rw) + size_t(e0) * D;
@@ -288,22 +286,18 @@ __global__ void __launch_bounds__(MD_THREADS, 1)
     __syncthreads();
     float* lg = reinterpret_cast<float*>(sm + L.o_lg);
     const uint16_t* rsrc = a.staged ? rws : rrows;
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
     for (int el = warp; el < ne; el += MD_WARPS) {
-        const float v = router_dot(xs, a.x_dt, rsrc + size_t(el) * D, a.rw_dt, D, lane);
-        if (lane == 0) lg[el] = v;
+        const float v = router_dot(xs, a.x_dt, rsrc + size_t(el) * D, a.rw_dt, D, lane);  // (in every lane)
+        if (lane < MD_CS) md_st_dsmem_f(map_peer(smem_u32(lg + e0 + el), uint32_t(lane)), v);  // lane p: into peer p
     }
-    cluster_sync();  // every CTA's logits are visible to the cluster
+    cluster_sync();  // every expert's logit is in every CTA's shared memory
     uint32_t* sel_i = reinterpret_cast<uint32_t*>(sm + L.o_sel);
     float* sel_w = reinterpret_cast<float*>(sm + L.o_sel) + k;
     uint32_t* xf = reinterpret_cast<uint32_t*>(sm + L.o_xf);
     float* sx = reinterpret_cast<float*>(sm + L.o_sx);
     if (warp == 0) {
-        const uint32_t base = smem_u32(lg);
-        auto get = [&](int e) {
-            const int owner = e / EC;
-            return ld_dsmem_f(map_peer(base + 4u * uint32_t(e - owner * EC), uint32_t(owner)));
-        };
-        score_and_select(get, E, k, a.mode, lane, sel_i, sel_w);
+        score_and_select([&](int e) { return lg[e]; }, E, k, a.mode, lane, sel_i, sel_w);
     } else {
         md_frags(xs, D / 64, xf, sx, tid - 32, MD_THREADS - 32, dt);
     }
@@ -415,26 +409,20 @@ __global__ void __launch_bounds__(MD_THREADS, 1)
             }
     }
     __syncthreads();
-    uint16_t* hm = reinterpret_cast<uint16_t*>(sm + L.o_hm);
+    // ---- the cluster's h slice: each CTA writes its R values into every peer's copy of the slice ----
+    uint16_t* hs = reinterpret_cast<uint16_t*>(sm + L.o_hs);
     for (int r = tid; r < R; r += MD_THREADS) {
         float gs = 0.0f, us = 0.0f;
         for (int w = 0; w < MD_WARPS; ++w) {
             gs += red[(w * 2) * RR + r];
             us += red[(w * 2 + 1) * RR + r];
         }
-        hm[r] = F16Traits<T>::from_f32(md_swiglu<T>(gs, us));
+        const uint16_t hv = F16Traits<T>::from_f32(md_swiglu<T>(gs, us));
+        const uint32_t dst = smem_u32(hs + t * R + r);
+#pragma unroll
+        for (int p = 0; p < MD_CS; ++p) md_st_dsmem_u16(map_peer(dst, uint32_t(p)), hv);
     }
-
-    // ---- the cluster's h slice through distributed shared memory ----
-    cluster_sync();
-    uint16_t* hs = reinterpret_cast<uint16_t*>(sm + L.o_hs);
-    const uint32_t hm_addr = smem_u32(hm);
-    for (int i = tid; i < L.KS; i += MD_THREADS) {
-        const int owner = i / R, idx = i - owner * R;
-        hs[i] = md_ld_dsmem_u16(map_peer(hm_addr + 2u * uint32_t(idx), uint32_t(owner)));
-    }
-    md_cluster_arrive();  // this CTA is done reading its peers' shared memory
-    __syncthreads();
+    cluster_sync();  // the whole slice in every CTA; no shared-memory access crosses CTAs after this
     uint32_t* hf = reinterpret_cast<uint32_t*>(sm + L.o_hf);
     float* hsx = reinterpret_cast<float*>(sm + L.o_hsx);
     md_frags(hs, gq, hf, hsx, tid, MD_THREADS, dt);
@@ -508,7 +496,6 @@ __global__ void __launch_bounds__(MD_THREADS, 1)
         }
         if (tid == 0) atomicExch(a.cnt + t, 0u);
     }
-    md_cluster_wait();  // peers have finished reading this CTA's h values
 }
 
 // ------------------------------------------------------------------------------------------------

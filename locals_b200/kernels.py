@@ -63,6 +63,21 @@ def _check_cuda(*ts: torch.Tensor) -> None:
             raise ValueError("locals_b200 kernels take contiguous tensors")
 
 
+def _check_format(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, K: int, bits: int,
+                  group_size: int) -> None:
+    """The MLX affine layout for rows of K inputs: w (..., K*bits/32) 32-bit words, scales and biases
+    (..., K/group_size) with the same leading dimensions (mx.quantized_matmul rejects mismatched shapes the same way).
+    The kernels read whole rows of K through raw pointers, so a mismatch is refused here, before any launch."""
+    if bits not in (4, 8) or K % group_size or (K * bits) % 32:
+        raise ValueError(f"K={K} does not fit {bits}-bit codes in groups of {group_size}")
+    if w.shape[-1] != K * bits // 32 or scales.shape[-1] != K // group_size:
+        raise ValueError(f"weights {tuple(w.shape)} / scales {tuple(scales.shape)} do not match K={K} at {bits} bits, "
+                         f"group {group_size}")
+    if tuple(scales.shape) != tuple(biases.shape) or tuple(w.shape[:-1]) != tuple(scales.shape[:-1]):
+        raise ValueError(f"weights {tuple(w.shape)}, scales {tuple(scales.shape)} and biases {tuple(biases.shape)} "
+                         "disagree on their rows")
+
+
 # ---- format ------------------------------------------------------------------------------------
 
 def quantize(w: torch.Tensor, group_size: int = 64, bits: int = 4, dtype: Optional[torch.dtype] = None):
@@ -141,6 +156,7 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, bia
     if choice is not None and tuple(choice) == ("auto",):  # the library's own choice, recorded by the tuner
         choice = None
     _check_cuda(x2, w, scales, biases)
+    _check_format(w, scales, biases, K, bits, group_size)
     if scales.dtype != x.dtype or biases.dtype != x.dtype:
         raise TypeError("scales and biases must have the activations' dtype")
     y = out if out is not None else torch.empty((M, N), dtype=x.dtype, device=x.device)
@@ -160,6 +176,7 @@ def qmm_split(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: to
     x2 = x.reshape(-1, K).contiguous()
     M, N = x2.shape[0], w.shape[0]
     _check_cuda(x2, w, scales, biases)
+    _check_format(w, scales, biases, K, bits, group_size)
     outs = [torch.empty((M, wd), dtype=x.dtype, device=x.device) for wd in widths]
     import ctypes
     ptrs = (ctypes.c_void_p * len(outs))(*[o.data_ptr() for o in outs])
@@ -179,6 +196,10 @@ def qmm_glu(x: torch.Tensor, gate: Tuple[torch.Tensor, torch.Tensor, torch.Tenso
     M = x2.shape[0]
     I = rows if rows is not None else gate[0].shape[0]
     _check_cuda(x2)
+    for m in (gate, up):
+        _check_format(*m, K, bits, group_size)
+        if m[0].shape[0] < I:
+            raise ValueError(f"{I} rows asked of a {m[0].shape[0]}-row matrix")
     h = torch.empty((M, I), dtype=x.dtype, device=x.device)
     call("lq_qmm_glu", x2.data_ptr(), gate[0].data_ptr(), gate[1].data_ptr(), gate[2].data_ptr(), up[0].data_ptr(),
          up[1].data_ptr(), up[2].data_ptr(), h.data_ptr(), M, I, K, bits, group_size, dtype_code(x.dtype),

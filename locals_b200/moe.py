@@ -17,7 +17,7 @@ import torch
 
 from . import _lib
 from ._lib import call
-from .kernels import _check_cuda, _stream, dtype_code
+from .kernels import _check_cuda, _check_format, _stream, dtype_code
 
 SOFTMAX, SIGMOID = 0, 1
 
@@ -107,6 +107,10 @@ def experts(xs: torch.Tensor, grouping, mats: Sequence, N: int, max_rows: int, b
     glu = len(mats) == 2
     w0, s0, b0 = mats[0]
     w1, s1, b1 = mats[1] if glu else (w0, s0, b0)
+    for w_, s_, b_ in mats:
+        _check_format(w_, s_, b_, K, bits, group_size)
+        if w_.dim() != 3 or w_.shape[0] != E or w_.shape[1] != N:
+            raise ValueError(f"expert stack {tuple(w_.shape)} is not ({E}, {N}, K*bits/32)")
     out = torch.empty((P, N), dtype=xs.dtype, device=xs.device)
     call("lq_moe_experts", xs.data_ptr(), starts.data_ptr(), experts_.data_ptr(), nseg.data_ptr(), P, max_rows,
          1 if glu else 0, w0.data_ptr(), s0.data_ptr(), b0.data_ptr(), w1.data_ptr(), s1.data_ptr(), b1.data_ptr(),
@@ -126,6 +130,7 @@ def down_combine(h: torch.Tensor, grouping, weights: torch.Tensor, down, bits: i
     w, s, b = down
     E, N = w.shape[0], w.shape[1]
     K = h.shape[-1]
+    _check_format(w, s, b, K, bits, group_size)
     y = torch.empty((1, N), dtype=h.dtype, device=h.device)
     rc = _lib.lib().lq_moe_down_combine(h.data_ptr(), experts_.data_ptr(), None if pos is None else pos.data_ptr(),
                                         weights.data_ptr(), w.data_ptr(), s.data_ptr(), b.data_ptr(), y.data_ptr(), k,
@@ -241,6 +246,11 @@ def decode(x: torch.Tensor, router_w: torch.Tensor, gate, up, down, k: int, mode
     D = x2.shape[1]
     E = router_w.shape[0]
     I = gate[0].shape[1]
+    for m in (gate, up):
+        _check_format(*m, D, bits, group_size)
+    _check_format(*down, I, bits, group_size)
+    if router_w.shape[-1] != D or any(m[0].shape[0] != E for m in (gate, up, down)) or down[0].shape[1] != D:
+        raise ValueError("router / expert stacks do not match the token width or the expert count")
     work = workspace if workspace is not None else decode_workspace(E, k, D, I, x2.device)
     if work is None:
         return None
