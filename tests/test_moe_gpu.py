@@ -149,6 +149,23 @@ def test_route_fused(cuda, T):
     np.testing.assert_allclose(w1.cpu().numpy(), w2.cpu().numpy(), rtol=1e-5, atol=1e-6)
 
 
+@pytest.mark.parametrize("T,E,k,mode", [(40, 64, 4, 0), (37, 20, 3, 1), (130, 128, 8, 0), (100, 64, 4, 1)])
+def test_route_batched_equals_one_token(cuda, T, E, k, mode):
+    """Batched routing (several tokens a warp: the cluster kernel up to 64 tokens, the tiled kernel above) keeps the
+    one-warp dot's summation order, so each token's experts and weights are bit-identical to routing it alone."""
+    import torch
+    from locals_b200 import moe
+
+    rng = np.random.default_rng(T + E)
+    x, wr = _router_inputs(rng, T, E, 2048)
+    xt, wt = x_torch(x, "bfloat16", cuda), torch.from_numpy(wr).to(cuda, torch.float16)
+    ib, wb = moe.route(xt, wt, k, mode)
+    for t in range(T):
+        i1, w1 = moe.route(xt[t:t + 1].contiguous(), wt, k, mode)
+        assert torch.equal(ib[t:t + 1], i1)
+        assert torch.equal(wb[t:t + 1], w1)
+
+
 @pytest.mark.parametrize("M", [1, 3])
 def test_direct_grouping_matches_sort(cuda, M):
     # one segment a (token, slot) pair (no counting sort, the decode path for one token) computes what the sorted
