@@ -650,6 +650,8 @@ CASES = {
     "mlp64": "8-bit MLP gate||up + SiLU.mul and down at M=64, 4 layers",
     "mlp1": "8-bit MLP gate||up + SiLU.mul and down at M=1, 4 layers (320 MB > L2)",
     "tc": "prefill GEMM x bf16 [1024,4096] . 4-bit [7168,4096]^T",
+    "moe1": "MoE layer at one token (the fused one-launch kernel), 64 experts top-4, D 2048, I 768, 16 distinct layers "
+            "(170 MB of routed weights > L2)",
     "moe16": "MoE layer, 64 experts top-4, D 2048, I 768, M=16",
     "moe512": "MoE layer, 64 experts top-4, D 2048, I 768, M=512",
     "kv8": "8-bit KV decode attention, B=8, 32 query heads on 4 kv heads, 32768 keys (285 MB cache > L2)",
@@ -686,6 +688,20 @@ def run_case(name):
         x = torch.randn((1024, 4096), generator=gen, device=dev).to(torch.bfloat16)
         for _ in range(4):
             kernels.quantized_matmul(x, w, s, b)
+    elif name == "moe1":
+        E, D, I = 64, 2048, 768
+
+        def stack(N, Kd):  # random packed codes, small positive scales (timing only)
+            wq = torch.randint(-2 ** 31, 2 ** 31 - 1, (E, N, Kd // 8), generator=gen, device=dev, dtype=torch.int32)
+            sc = (torch.rand((E, N, Kd // 64), generator=gen, device=dev) * 2e-3 + 5e-4).to(torch.bfloat16)
+            return wq, sc, (-8.0 * sc.float()).to(torch.bfloat16)
+
+        layers = [moe.MoELayer((torch.randn((E, D), generator=gen, device=dev) * 0.02).to(torch.float16),
+                               stack(I, D), stack(I, D), stack(D, I), top_k=4) for _ in range(16)]
+        x = torch.randn((1, D), generator=gen, device=dev).to(torch.bfloat16)
+        for _ in range(3):
+            for la in layers:
+                la(x)
     elif name in ("moe16", "moe512"):
         E, D, I = 64, 2048, 768
 
