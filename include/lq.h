@@ -245,6 +245,19 @@ int lq_ipc_export(const void* ptr, void* handle, size_t* offset);
 int lq_ipc_import(const void* handle, size_t offset, void** ptr);
 int lq_ipc_close(void* ptr, size_t offset);
 
+/* The exchange between column shards at decode sizes without NCCL (no counterpart in the reference, which runs on one
+ * GPU; it replaces the all-gather after a column-sharded projection): copies this rank's row-major (M, n) block src
+ * into columns [col_off, col_off + n) of every rank's (M, ldo) buffer dst[0 .. G) (dst[rank] this GPU's own, the
+ * others peers' buffers from lq_ipc_import), then meets the other ranks on flags: when the launch ends, dst[rank]
+ * holds every rank's columns. sync[p] is rank p's sync block (lq_peer_sync_bytes() bytes, zero-filled before first
+ * use, exported and imported like the buffers; sync[rank] this rank's own). Ranks on distinct GPUs (G <= 8), the
+ * same calls in the same order on every rank, and buffers reused no sooner than every second call (a peer may be one
+ * call ahead). elem_bytes 2 or 4; n, col_off and ldo in 16-byte multiples. A peer that does not arrive within one
+ * second leaves LQ_DEV_TIMEOUT in the device status. */
+size_t lq_peer_sync_bytes(void);
+int lq_peer_gather_cols(const void* src, int M, int n, int col_off, int ldo, int elem_bytes, void* const* dst, int G,
+                        int rank, void* const* sync, void* stream);
+
 /* 1 if kernel family `family` (LQ_FAM_*; LQ_FAM_AUTO = any) accepts this shape and format, else 0. Host-only,
  * needs no GPU. Replaces the per-family supported(M, K, N, cfg) predicates the reference's tuner filters
  * its candidates with (locals/qmv_frag.py:162,519; locals/nax_kernel.py:399-408; locals/kernels.py:654-674). */

@@ -71,6 +71,9 @@ size_t moe_decode_workspace_bytes(int E, int k, int D, int I);
 int moe_decode_run(const void* x, int x_dt, const void* rw, int rw_dt, int E, int k, int mode, const uint32_t* const* w,
                    const void* const* s, const void* const* b, int D, int I, void* y, uint32_t* inds, float* wts,
                    void* work, size_t work_bytes, cudaStream_t st);
+size_t peer_sync_bytes();
+int peer_gather_run(const void* src, int M, int n, int col_off, int ldo, int elem_bytes, void* const* dst, int G,
+                    int rank, void* const* sync, cudaStream_t st);
 bool kv_attend_shape_ok(int B, int H, int KVH, int n, int cap, int head_dim);
 size_t kv_attend_workspace_bytes(int B, int H, int KVH, int n, int sms);
 int kv_attend_run(const void* q, const uint32_t* kq, const void* ks, const void* kb, const uint32_t* vq,
@@ -473,6 +476,17 @@ int lq_moe_decode(const void* x, const void* router_w, int router_dtype, int E, 
     const void* b[3] = {bg, bu, bd};
     return finish(moe_decode_run(x, dtype, router_w, router_dtype, E, k, mode, w, s, b, D, I, y, inds, weights,
                                  workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+size_t lq_peer_sync_bytes(void) { return peer_sync_bytes(); }
+
+int lq_peer_gather_cols(const void* src, int M, int n, int col_off, int ldo, int elem_bytes, void* const* dst, int G,
+                        int rank, void* const* sync, void* stream) {
+    if (!src || !dst || !sync) return LQ_E_ARG;
+    int rc = check_device();
+    if (rc) return rc;
+    return finish(peer_gather_run(src, M, n, col_off, ldo, elem_bytes, dst, G, rank, sync,
+                                  reinterpret_cast<cudaStream_t>(stream)));
 }
 
 int lq_add_rms_norm(const void* x, const void* r, const void* w, void* h, void* n, int rows, int D, float eps,

@@ -154,6 +154,99 @@ class PeerOutputs:
         self._opened = []
 
 
+def _distinct_gpus(group=None) -> bool:
+    """True when every rank of the group drives its own GPU (a collective: every rank calls it). Ranks sharing a GPU
+    must not meet on flags inside kernels (nothing makes their kernels run at the same time)."""
+    G, _ = _world(group)
+    props = torch.cuda.get_device_properties(torch.cuda.current_device())
+    ids = [None] * G
+    dist.all_gather_object(ids, str(getattr(props, "uuid", "")) or str(torch.cuda.current_device()), group=group)
+    return len(set(ids)) == G
+
+
+class PeerSync:
+    """This rank's sync block of the peer gather (lq_peer_sync_bytes() bytes, zero-filled: the flags the other ranks
+    store into, a round counter and a CTA counter), mapped into every rank's process through CUDA IPC. Creating one is
+    a collective."""
+
+    def __init__(self, device, group=None):
+        import ctypes
+
+        from . import _lib
+
+        G, r = _world(group)
+        self.block = torch.zeros(int(_lib.lib().lq_peer_sync_bytes()), dtype=torch.uint8, device=device)
+        h = (ctypes.c_char * 64)()
+        off = ctypes.c_size_t()
+        _lib.call("lq_ipc_export", self.block.data_ptr(), h, ctypes.byref(off))
+        handles = [None] * G
+        dist.all_gather_object(handles, (bytes(h), int(off.value)), group=group)
+        self.ptrs, self._opened = [], []
+        for p, (hb, o) in enumerate(handles):
+            if p == r:
+                self.ptrs.append(self.block.data_ptr())
+                continue
+            ptr = ctypes.c_void_p()
+            _lib.call("lq_ipc_import", (ctypes.c_char * 64).from_buffer_copy(hb), o, ctypes.byref(ptr))
+            self.ptrs.append(int(ptr.value))
+            self._opened.append((int(ptr.value), o))
+
+    def close(self) -> None:
+        import ctypes
+
+        from . import _lib
+
+        for ptr, o in self._opened:
+            _lib.lib().lq_ipc_close(ctypes.c_void_p(ptr), o)
+        self._opened = []
+
+
+class PeerGather:
+    """The all-gather of a column-sharded (M, N/G) result at decode sizes without NCCL (lq_peer_gather_cols): one
+    kernel stores this rank's columns into every rank's (M, N) buffer over peer memory and meets the other ranks on
+    flags. Needs every rank on its own GPU (checked once, a collective); otherwise ``ok`` is False and the caller
+    uses the NCCL all-gather. Buffers are created per (M, N, dtype) on first use (a collective: every rank makes the same
+    calls in the same order) and used in turn; a returned tensor is overwritten two gathers of that shape later."""
+
+    def __init__(self, group=None):
+        G, r = _world(group)
+        self.G, self.rank, self.group = G, r, group
+        self.ok = 1 < G <= FUSED_GATHER_MAX_RANKS and _distinct_gpus(group)
+        self._bufs = {}
+        self._sync = None
+
+    def __call__(self, y_local: torch.Tensor) -> torch.Tensor:
+        import ctypes
+
+        from . import _lib
+
+        y_local = y_local.contiguous()
+        M, Nl = y_local.shape
+        N = Nl * self.G
+        key = (M, N, y_local.dtype)
+        if self._sync is None:
+            self._sync = PeerSync(y_local.device, self.group)
+        if key not in self._bufs:
+            self._bufs[key] = PeerOutputs((M, N), y_local.dtype, y_local.device, self.group)
+        y, addrs = self._bufs[key].next()
+        dst = (ctypes.c_void_p * self.G)(*addrs)
+        sync = (ctypes.c_void_p * self.G)(*self._sync.ptrs)
+        _lib.call("lq_peer_gather_cols", y_local.data_ptr(), M, Nl, self.rank * Nl, N, y_local.element_size(), dst,
+                  self.G, self.rank, sync, torch.cuda.current_stream().cuda_stream)
+        return y
+
+    def close(self) -> None:
+        for b in self._bufs.values():
+            b.close()
+        if self._sync is not None:
+            self._sync.close()
+
+
+def gather_ok(y_local: torch.Tensor) -> bool:
+    """The peer gather's layout: 16-byte column blocks."""
+    return y_local.is_cuda and (y_local.shape[1] * y_local.element_size()) % 16 == 0
+
+
 class ColumnShardedLinear:
     def __init__(self, full: QuantizedLinear, group=None, ops: Optional[Ops] = None, fused_gather: bool = True):
         self.group = group
@@ -166,6 +259,7 @@ class ColumnShardedLinear:
         self.fused_gather = fused_gather and ops is None
         self._peer = {}
         self._flag = None
+        self._pg = PeerGather(group) if (self.fused_gather and G > 1 and torch.cuda.is_available()) else None
 
     def _fused_ok(self, x2: torch.Tensor) -> bool:
         from . import kernels
@@ -208,6 +302,8 @@ class ColumnShardedLinear:
         if self._fused_ok(x2):
             return self._gather_dense(x2).reshape(*x.shape[:-1], -1)
         y = self.ops.qmm(x2, (self.local.weight, self.local.scales, self.local.biases), self.local.bits)
+        if self._pg is not None and self._pg.ok and gather_ok(y):
+            return self._pg(y).reshape(*x.shape[:-1], -1)
         return all_gather_cols(y, self.group).reshape(*x.shape[:-1], -1)
 
 
@@ -260,11 +356,18 @@ class ShardedMLP:
         self.down = tuple(_split_rows(t, G, r) for t in (down.weight, down.scales, down.biases))
         self.bits = gate.bits
         self.ops = ops or kernel_ops()
+        # the two exchanges over peer memory when every rank has its own GPU (kernel ops only), else NCCL
+        self._pg = PeerGather(group) if (ops is None and G > 1 and torch.cuda.is_available()) else None
+
+    def _gather(self, t: torch.Tensor) -> torch.Tensor:
+        if self._pg is not None and self._pg.ok and gather_ok(t):
+            return self._pg(t)
+        return all_gather_cols(t, self.group)
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         x2 = x.reshape(-1, x.shape[-1])
-        h = all_gather_cols(self.ops.glu(x2, self.gate, self.up, self.bits), self.group)
-        y = all_gather_cols(self.ops.qmm(h, self.down, self.bits), self.group)
+        h = self._gather(self.ops.glu(x2, self.gate, self.up, self.bits))
+        y = self._gather(self.ops.qmm(h, self.down, self.bits))
         return y.reshape(*x.shape[:-1], -1)
 
 

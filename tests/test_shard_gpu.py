@@ -60,6 +60,23 @@ def _worker(rank, world, port, path):
                                     / refp.abs().max())
         for pb in fused._peer.values():
             pb.close()
+        # decode-size column gather over peer memory (lq_peer_gather_cols): exact, five calls in a row (both buffers of
+        # each shape, the round flags advancing), two shapes interleaved as a sharded MLP uses them
+        from locals_b200.shard import PeerGather
+
+        pg = PeerGather()
+        assert pg.ok
+        bad = 0
+        for it in range(5):
+            for M_, n_ in ((1, 512), (16, 1024)):
+                mine = torch.full((M_, n_), float(rank * 100 + it), device=dev).to(torch.bfloat16)
+                mine[:, 0] = float(it)
+                got = pg(mine)
+                want = torch.cat([torch.full((M_, n_), float(p_ * 100 + it), device=dev) for p_ in range(world)], 1)
+                want[:, ::n_] = float(it)
+                bad += int((got.float() != want).sum())
+        errs["peer_gather_mismatches"] = float(bad)
+        pg.close()
         g, u, d = (QuantizedLinear(*layer(1024, 2048, 8), bits=8), QuantizedLinear(*layer(1024, 2048, 8), bits=8),
                    QuantizedLinear(*layer(2048, 1024, 8), bits=8))
         h = kernels.qmm_glu(x, (g.weight, g.scales, g.biases), (u.weight, u.scales, u.biases), bits=8)
@@ -98,5 +115,6 @@ def test_sharded_two_gpus(tmp_path):
     mp.spawn(_worker, args=(2, _port(), path), nprocs=2, join=True)
     for errs in torch.load(path):
         assert errs.pop("status") == 0
+        assert errs.pop("peer_gather_mismatches") == 0
         for name, e in errs.items():
             assert e <= 1e-2, (name, e)
