@@ -431,8 +431,9 @@ def _timed_max(torch, fn, steps, warmup, stream, dist):
 
 
 def bench_sharded(torch, dist, ws, steps, warmup, dev, stream):
-    """cfg3, cfg4, cfg5 split over the ranks (column shards + all-gather, experts +
-    all-to-all), each step captured in a CUDA graph with its NCCL collectives; returns rank-0 results."""
+    """cfg3, cfg4, cfg5 split over the ranks (column shards + all-gather, expert parallelism), the exchanges over peer
+    memory (CUDA IPC buffers, flags; NCCL only where ranks share a GPU), each step captured in a CUDA graph; returns
+    rank-0 results."""
     from locals_b200 import moe
     from locals_b200.kernels import QuantizedLinear
     from locals_b200.shard import ExpertParallelMoE, ShardedMLP, ColumnShardedLinear
@@ -440,36 +441,41 @@ def bench_sharded(torch, dist, ws, steps, warmup, dev, stream):
     out = {}
     gen = torch.Generator(device=dev)
     gen.manual_seed(2)
-    g_ = QuantizedLinear(*make_layer(torch, 9728, 2560, 8, torch.bfloat16, gen, dev), bits=8)
-    u_ = QuantizedLinear(*make_layer(torch, 9728, 2560, 8, torch.bfloat16, gen, dev), bits=8)
-    d_ = QuantizedLinear(*make_layer(torch, 2560, 9728, 8, torch.bfloat16, gen, dev), bits=8)
-    mlp = ShardedMLP(g_, u_, d_)
-    del g_, u_, d_
+    mlps = []
+    for _ in range(4):  # as the one-GPU config-3 bench: four distinct MLPs a step
+        g_ = QuantizedLinear(*make_layer(torch, 9728, 2560, 8, torch.bfloat16, gen, dev), bits=8)
+        u_ = QuantizedLinear(*make_layer(torch, 9728, 2560, 8, torch.bfloat16, gen, dev), bits=8)
+        d_ = QuantizedLinear(*make_layer(torch, 2560, 9728, 8, torch.bfloat16, gen, dev), bits=8)
+        mlps.append(ShardedMLP(g_, u_, d_))
+        del g_, u_, d_
     out["cfg3_mlp_8bit_sharded"] = {}
     for M in (1, 16, 64):
         x = torch.randn((M, 2560), generator=gen, device=dev).to(torch.bfloat16)
-        ms = _timed_max(torch, lambda: mlp(x), steps, warmup, stream, dist)
+        ms = _timed_max(torch, lambda: [m(x) for m in mlps], steps, warmup, stream, dist) / len(mlps)
         out["cfg3_mlp_8bit_sharded"][f"M={M}"] = {"us_per_mlp": round(ms * 1e3, 2), "tok/s": round(M / (ms * 1e-3), 1)}
-    del mlp
+    del mlps
     gen.manual_seed(3)
     E, D, I = 64, 2048, 768
 
-    def stack(N, Kd):
-        ws_ = [make_layer(torch, N, Kd, 4, torch.bfloat16, gen, dev) for _ in range(E)]
-        return tuple(torch.stack([w[i] for w in ws_]).contiguous() for i in range(3))
+    def stack(N, Kd):  # random packed codes, small positive scales (as the one-GPU config-4 bench)
+        wq = torch.randint(-2 ** 31, 2 ** 31 - 1, (E, N, Kd // 8), generator=gen, device=dev, dtype=torch.int32)
+        sc = (torch.rand((E, N, Kd // 64), generator=gen, device=dev) * 2e-3 + 5e-4).to(torch.bfloat16)
+        return wq, sc, (-8.0 * sc.float()).to(torch.bfloat16)
 
-    gate, up, down = stack(I, D), stack(I, D), stack(D, I)
-    wr = (torch.randn((E, D), generator=gen, device=dev) * 0.02).to(torch.float16)
-    ep = ExpertParallelMoE(wr, gate, up, down, top_k=4)
-    del gate, up, down
+    eps = []
+    for _ in range(4):  # distinct layers a step (each rank holds its E/G experts of each)
+        wr = (torch.randn((E, D), generator=gen, device=dev) * 0.02).to(torch.float16)
+        eps.append(ExpertParallelMoE(wr, stack(I, D), stack(I, D), stack(D, I), top_k=4))
     out["cfg4_moe_ep"] = {}
     for M in (8, 64, 512):
         if M % ws:
             continue
+        L = 4 if M <= 16 else 2
         x = torch.randn((M // ws, D), generator=gen, device=dev).to(torch.bfloat16)
-        ms = _timed_max(torch, lambda: ep(x), steps, warmup, stream, dist)
-        out["cfg4_moe_ep"][f"M={M}"] = {"us_per_layer": round(ms * 1e3, 2), "tok/s": round(M / (ms * 1e-3), 1)}
-    del ep
+        ms = _timed_max(torch, lambda: [e(x) for e in eps[:L]], steps, warmup, stream, dist) / L
+        out["cfg4_moe_ep"][f"M={M}"] = {"us_per_layer": round(ms * 1e3, 2), "tok/s": round(M / (ms * 1e-3), 1),
+                                        "layers_rotated": L}
+    del eps
     gen.manual_seed(4)
     full = QuantizedLinear(*make_layer(torch, 14336, 4096, 4, torch.bfloat16, gen, dev))
     lin = ColumnShardedLinear(full)  # the GEMM stores its output tiles into every rank's buffer (fused all-gather)
@@ -619,7 +625,7 @@ def run_gpu(args):
                        "layers_per_step": head_layers, "weights_per_step_MB": round(head["bytes_per_step"] / 1e6, 1),
                        "l2": "inputs larger than L2 (distinct weights per layer, 318 MB per step)",
                        "parallelism": (f"{ws} replicas of the config-2 layer stack (weak); configs 3-5 sharded "
-                                       "with NCCL in the cfg*_sharded / cfg4_moe_ep keys") if ws > 1 else "1 GPU",
+                                       "over peer memory in the cfg*_sharded / cfg4_moe_ep keys") if ws > 1 else "1 GPU",
                        "graph": "CUDA graph of the step, PDL between launches"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "traffic": traffic,

@@ -125,6 +125,14 @@ int lq_moe_route(const void* x, int x_dtype, const void* w, int w_dtype, int T, 
 int lq_moe_group(const uint32_t* inds, int P, int E, int32_t* order, int32_t* starts, int32_t* experts, int32_t* nseg,
                  int32_t* pos, void* stream);
 
+/* The same counting sort over only the pairs routed to experts [lo, lo + range) (one rank's experts in an
+ * expert-parallel layer; no counterpart in the reference, which runs on one GPU): they are grouped under local ids
+ * 0 .. range - 1 in the stable order of lq_moe_group, every other pair under the padding bucket `range`, which sorts
+ * last and which lq_moe_experts skips (pass E = range there). starts (min(range + 1, P) + 1), experts and order as
+ * lq_moe_group; range <= 8191. */
+int lq_moe_group_range(const uint32_t* inds, int P, int lo, int range, int32_t* order, int32_t* starts,
+                       int32_t* experts, int32_t* nseg, int32_t* pos, void* stream);
+
 /* xs (P, D) = x[order[j] / k] for j < P: the tokens of the pairs in expert order (16-bit x, D % 8 == 0). */
 int lq_moe_gather(const void* x, const int32_t* order, int P, int k, int D, void* xs, void* stream);
 
@@ -257,6 +265,16 @@ int lq_ipc_close(void* ptr, size_t offset);
 size_t lq_peer_sync_bytes(void);
 int lq_peer_gather_cols(const void* src, int M, int n, int col_off, int ldo, int elem_bytes, void* const* dst, int G,
                         int rank, void* const* sync, void* stream);
+
+/* The combine-side exchange of an expert-parallel MoE layer over peer memory (no counterpart in the reference): row
+ * j of src (R, row_bytes) -- the rows this rank's grouped expert kernels wrote, those before the padding bucket of
+ * a lq_moe_group_range grouping (starts, experts, nseg, bucket = range; read on the device) -- goes to row idx[j]
+ * (the grouping's order: its pair index) of every rank's (dst_rows, row_bytes) buffer dst[0 .. G); then the ranks meet
+ * on the sync blocks as in lq_peer_gather_cols. rows_max bounds the rows sent (sizes the launch); row_bytes a
+ * multiple of 16. */
+int lq_peer_scatter_rows(const void* src, const int32_t* idx, const int32_t* starts, const int32_t* experts,
+                         const int32_t* nseg, int bucket, int rows_max, int row_bytes, int dst_rows, void* const* dst,
+                         int G, int rank, void* const* sync, void* stream);
 
 /* 1 if kernel family `family` (LQ_FAM_*; LQ_FAM_AUTO = any) accepts this shape and format, else 0. Host-only,
  * needs no GPU. Replaces the per-family supported(M, K, N, cfg) predicates the reference's tuner filters

@@ -40,6 +40,9 @@ SIGNATURES = {
     "lq_moe_down_combine": ([_vp, _vp, _vp, _vp, _u32p, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp], _i),
     "lq_moe_decode_workspace": ([_i, _i, _i, _i], ctypes.c_size_t),
     "lq_peer_sync_bytes": ([], ctypes.c_size_t),
+    "lq_peer_scatter_rows": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, ctypes.POINTER(ctypes.c_void_p), _i, _i,
+                              ctypes.POINTER(ctypes.c_void_p), _vp], _i),
+    "lq_moe_group_range": ([_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp], _i),
     "lq_peer_gather_cols": ([_vp, _i, _i, _i, _i, _i, ctypes.POINTER(ctypes.c_void_p), _i, _i,
                              ctypes.POINTER(ctypes.c_void_p), _vp], _i),
     "lq_moe_decode": ([_vp, _vp, _i, _i, _i, _i, _u32p, _vp, _vp, _u32p, _vp, _vp, _u32p, _vp, _vp, _i, _i, _i, _i, _i,

@@ -72,6 +72,11 @@ int moe_decode_run(const void* x, int x_dt, const void* rw, int rw_dt, int E, in
                    const void* const* s, const void* const* b, int D, int I, void* y, uint32_t* inds, float* wts,
                    void* work, size_t work_bytes, cudaStream_t st);
 size_t peer_sync_bytes();
+int peer_scatter_rows_run(const void* src, const int32_t* idx, const int32_t* starts, const int32_t* experts,
+                          const int32_t* nseg, int bucket, int rows_max, int row_bytes, int dst_rows,
+                          void* const* dst, int G, int rank, void* const* sync, cudaStream_t st);
+int group_range_run(const uint32_t* inds, int P, int lo, int range, int32_t* order, int32_t* starts, int32_t* experts,
+                    int32_t* nseg, int32_t* pos, cudaStream_t st);
 int peer_gather_run(const void* src, int M, int n, int col_off, int ldo, int elem_bytes, void* const* dst, int G,
                     int rank, void* const* sync, cudaStream_t st);
 bool kv_attend_shape_ok(int B, int H, int KVH, int n, int cap, int head_dim);
@@ -479,6 +484,26 @@ int lq_moe_decode(const void* x, const void* router_w, int router_dtype, int E, 
 }
 
 size_t lq_peer_sync_bytes(void) { return peer_sync_bytes(); }
+
+int lq_peer_scatter_rows(const void* src, const int32_t* idx, const int32_t* starts, const int32_t* experts,
+                         const int32_t* nseg, int bucket, int rows_max, int row_bytes, int dst_rows, void* const* dst,
+                         int G, int rank, void* const* sync, void* stream) {
+    if (!src || !idx || !starts || !experts || !nseg || !dst || !sync) return LQ_E_ARG;
+    int rc = check_device();
+    if (rc) return rc;
+    return finish(peer_scatter_rows_run(src, idx, starts, experts, nseg, bucket, rows_max, row_bytes, dst_rows, dst,
+                                        G, rank, sync, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int lq_moe_group_range(const uint32_t* inds, int P, int lo, int range, int32_t* order, int32_t* starts,
+                       int32_t* experts, int32_t* nseg, int32_t* pos, void* stream) {
+    if (!inds || !order || !starts || !experts || !nseg) return LQ_E_ARG;
+    if (P < 1 || lo < 0 || range < 1 || range > 8191) return LQ_E_SHAPE;
+    int rc = check_device();
+    if (rc) return rc;
+    return finish(group_range_run(inds, P, lo, range, order, starts, experts, nseg, pos,
+                                  reinterpret_cast<cudaStream_t>(stream)));
+}
 
 int lq_peer_gather_cols(const void* src, int M, int n, int col_off, int ldo, int elem_bytes, void* const* dst, int G,
                         int rank, void* const* sync, void* stream) {

@@ -74,8 +74,17 @@ constexpr int GROUP_STAGE = 8192;  // routed pairs staged in shared memory per r
 // histogram, a one-warp scan that emits the segments, then a one-warp pass over the pairs in order, 32 at a
 // time: __match_any_sync finds the lanes of the same expert, a pair's rank is the expert's running count
 // plus its rank among those lanes.
+// The expert a pair is grouped under: its own id, or with a range (range > 0) its id inside [lo, lo + range) and
+// `range` -- the padding bucket, which the grouped expert kernels skip -- for every expert outside it (the local
+// experts of one rank of an expert-parallel layer).
+__device__ __forceinline__ uint32_t grp_key(uint32_t e, int lo, int range) {
+    if (range <= 0) return e;
+    const uint32_t d = e - uint32_t(lo);
+    return d < uint32_t(range) ? d : uint32_t(range);
+}
+
 __global__ void group_kernel(const uint32_t* inds, int P, int E, int32_t* order, int32_t* starts, int32_t* experts,
-                             int32_t* nseg, int32_t* pos) {
+                             int32_t* nseg, int32_t* pos, int lo, int range) {
     grid_dep_wait();
     grid_dep_launch();
     extern __shared__ int32_t sh[];
@@ -86,7 +95,7 @@ __global__ void group_kernel(const uint32_t* inds, int P, int E, int32_t* order,
     for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
     for (int p = threadIdx.x; p < P; p += blockDim.x) {
-        const uint32_t e = inds[p];
+        const uint32_t e = grp_key(inds[p], lo, range);
         if (e < uint32_t(E))
             atomicAdd(&cnt[e], 1);
         else
@@ -122,7 +131,7 @@ __global__ void group_kernel(const uint32_t* inds, int P, int E, int32_t* order,
     for (int p0 = 0; p0 < P; p0 += GROUP_STAGE) {
         const int n = P - p0 < GROUP_STAGE ? P - p0 : GROUP_STAGE;
         __syncthreads();
-        for (int i = threadIdx.x; i < n; i += blockDim.x) staged[i] = inds[p0 + i];
+        for (int i = threadIdx.x; i < n; i += blockDim.x) staged[i] = grp_key(inds[p0 + i], lo, range);
         __syncthreads();
         if (threadIdx.x < 32) {
             for (int c = 0; c < n; c += 32) {
@@ -153,7 +162,7 @@ constexpr int GROUP_PAR_MAX_E = 1024;
 
 __global__ void __launch_bounds__(1024) group_par_kernel(const uint32_t* inds, int P, int E, int32_t* order,
                                                          int32_t* starts, int32_t* experts, int32_t* nseg,
-                                                         int32_t* pos) {
+                                                         int32_t* pos, int lo, int range) {
     grid_dep_wait();
     grid_dep_launch();
     extern __shared__ int32_t sh[];
@@ -167,7 +176,7 @@ __global__ void __launch_bounds__(1024) group_par_kernel(const uint32_t* inds, i
     __syncthreads();
     for (int c = p0; c < p1; c += 32) {
         const int p = c + lane;
-        const uint32_t e = p < p1 ? inds[p] : 0xFFFFFFFFu;
+        const uint32_t e = p < p1 ? grp_key(inds[p], lo, range) : 0xFFFFFFFFu;
         if (p < p1 && e >= uint32_t(E)) record_status(LQ_DEV_BOUNDS);
         const bool valid = p < p1 && e < uint32_t(E);
         const unsigned peers = __match_any_sync(0xFFFFFFFFu, valid ? e : 0xFFFFFFFFu);
@@ -214,7 +223,7 @@ __global__ void __launch_bounds__(1024) group_par_kernel(const uint32_t* inds, i
     __syncthreads();
     for (int c = p0; c < p1; c += 32) {
         const int p = c + lane;
-        const uint32_t e = p < p1 ? inds[p] : 0xFFFFFFFFu;
+        const uint32_t e = p < p1 ? grp_key(inds[p], lo, range) : 0xFFFFFFFFu;
         const bool valid = p < p1 && e < uint32_t(E);
         const unsigned peers = __match_any_sync(0xFFFFFFFFu, valid ? e : 0xFFFFFFFFu);
         const int rank = __popc(peers & ((1u << lane) - 1u));
@@ -496,8 +505,8 @@ int route_topk_run(const float* logits, int T, int E, int k, int mode, uint32_t*
     return launch_pdl(route_topk_kernel, dim3((T + 3) / 4), dim3(128), 0, st, logits, T, E, k, mode, inds, weights);
 }
 
-int group_run(const uint32_t* inds, int P, int E, int32_t* order, int32_t* starts, int32_t* experts, int32_t* nseg,
-              int32_t* pos, cudaStream_t st) {
+static int group_impl(const uint32_t* inds, int P, int E, int32_t* order, int32_t* starts, int32_t* experts,
+                      int32_t* nseg, int32_t* pos, cudaStream_t st, int lo, int range) {
     if (E <= GROUP_PAR_MAX_E && P > 256) {  // (up to 256 pairs the one-warp placement is as fast)
         const size_t smem = size_t(34) * E * sizeof(int32_t);
         if (smem > 48 * 1024) {
@@ -506,14 +515,27 @@ int group_run(const uint32_t* inds, int P, int E, int32_t* order, int32_t* start
             if (e != cudaSuccess) return LQ_E_CUDA;
         }
         return launch_pdl(group_par_kernel, dim3(1), dim3(1024), smem, st, inds, P, E, order, starts, experts, nseg,
-                          pos);
+                          pos, lo, range);
     }
     const size_t smem = size_t(2) * E * sizeof(int32_t) + size_t(GROUP_STAGE) * sizeof(uint32_t);
     if (smem > 48 * 1024) {
         const cudaError_t e = cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
         if (e != cudaSuccess) return LQ_E_CUDA;
     }
-    return launch_pdl(group_kernel, dim3(1), dim3(1024), smem, st, inds, P, E, order, starts, experts, nseg, pos);
+    return launch_pdl(group_kernel, dim3(1), dim3(1024), smem, st, inds, P, E, order, starts, experts, nseg, pos, lo,
+                      range);
+}
+
+int group_run(const uint32_t* inds, int P, int E, int32_t* order, int32_t* starts, int32_t* experts, int32_t* nseg,
+              int32_t* pos, cudaStream_t st) {
+    return group_impl(inds, P, E, order, starts, experts, nseg, pos, st, 0, 0);
+}
+
+// The grouping of the pairs routed to experts [lo, lo + range) only (local ids 0 .. range - 1); every other pair goes
+// to the padding bucket `range`, which sorts last.
+int group_range_run(const uint32_t* inds, int P, int lo, int range, int32_t* order, int32_t* starts, int32_t* experts,
+                    int32_t* nseg, int32_t* pos, cudaStream_t st) {
+    return group_impl(inds, P, range + 1, order, starts, experts, nseg, pos, st, lo, range);
 }
 
 int gather_rows_run(const void* x, const int32_t* order, int P, int k, int D, void* xs, cudaStream_t st) {

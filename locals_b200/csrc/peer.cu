@@ -50,27 +50,14 @@ __device__ __forceinline__ uint32_t peer_ld_acquire(const uint32_t* p) {
     return v;
 }
 
-__global__ void __launch_bounds__(256) peer_gather_kernel(const uint4* __restrict__ src, const PeerPtrs dst,
-                                                          const PeerPtrs sync, int G, int rank, int M, int pieces_row,
-                                                          int ld_pieces, int off_pieces) {
-    grid_dep_wait();  // src is the previous kernel's output
-    // the next kernel may launch now and stream its own weights during the exchange: it waits for this grid's end
-    // (griddepcontrol.wait) before it reads the gathered buffer
-    grid_dep_launch();
-    const int64_t total = int64_t(M) * pieces_row;
-    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
-        const int64_t m = i / pieces_row, c = i - m * pieces_row;
-        const uint4 v = src[i];
-        const int64_t off = m * ld_pieces + off_pieces + c;
-#pragma unroll
-        for (int d = 0; d < PEER_MAX; ++d)
-            if (d < G) reinterpret_cast<uint4*>(dst.p[d])[off] = v;
-    }
+// After a CTA's stores: its thread 0 counts the CTA in (device-scope acquire/release on this rank's counter); the last
+// CTA takes the next round, releases it into its slot of every peer's flag array (system scope: with the counter's
+// chain it orders every CTA's stores before the flag for the peer that acquires it) and waits -- bounded by one second
+// of %globaltimer, then LQ_DEV_TIMEOUT -- until every peer's slot of its own array holds that round.
+__device__ __forceinline__ void peer_meet(const PeerPtrs& sync, int G, int rank) {
     __syncthreads();  // every store of this CTA before thread 0's release (cumulative) and count
     if (threadIdx.x != 0) return;
     uint32_t* own = reinterpret_cast<uint32_t*>(sync.p[rank]);
-    // device-scope release / acquire on the counter, then the last CTA's system-scope release of each flag: the
-    // chain orders every CTA's peer stores before the flag for the peer that acquires it
     uint32_t prev;
     asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(own + PEER_DONE_OFF) : "memory");
     if (prev != gridDim.x - 1) return;
@@ -90,6 +77,56 @@ __global__ void __launch_bounds__(256) peer_gather_kernel(const uint4* __restric
             __nanosleep(64);
         }
     }
+}
+
+__global__ void __launch_bounds__(256) peer_gather_kernel(const uint4* __restrict__ src, const PeerPtrs dst,
+                                                          const PeerPtrs sync, int G, int rank, int M, int pieces_row,
+                                                          int ld_pieces, int off_pieces) {
+    grid_dep_wait();  // src is the previous kernel's output
+    // the next kernel may launch now and stream its own weights during the exchange: it waits for this grid's end
+    // (griddepcontrol.wait) before it reads the gathered buffer
+    grid_dep_launch();
+    const int64_t total = int64_t(M) * pieces_row;
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t m = i / pieces_row, c = i - m * pieces_row;
+        const uint4 v = src[i];
+        const int64_t off = m * ld_pieces + off_pieces + c;
+#pragma unroll
+        for (int d = 0; d < PEER_MAX; ++d)
+            if (d < G) reinterpret_cast<uint4*>(dst.p[d])[off] = v;
+    }
+    peer_meet(sync, G, rank);
+}
+
+// Rows of an expert-parallel layer's local results to every rank: src row j (j < the number of pairs this rank
+// computed: the rows before the grouping's padding bucket) goes to row idx[j] (its pair index) of every rank's buffer.
+// One thread a 16-byte piece of a row.
+__global__ void __launch_bounds__(256) peer_scatter_rows_kernel(const uint4* __restrict__ src,
+                                                                const int32_t* __restrict__ idx,
+                                                                const int32_t* __restrict__ starts,
+                                                                const int32_t* __restrict__ experts,
+                                                                const int32_t* __restrict__ nseg, int bucket,
+                                                                int dst_rows, const PeerPtrs dst, const PeerPtrs sync,
+                                                                int G, int rank, int pieces_row) {
+    grid_dep_wait();  // src, idx and the grouping come from the previous kernels
+    grid_dep_launch();
+    const int ns = *nseg;
+    const int rows = (ns > 0 && experts[ns - 1] == bucket) ? starts[ns - 1] : starts[ns];
+    const int64_t total = int64_t(rows) * pieces_row;
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t j = i / pieces_row, c = i - j * pieces_row;
+        const int r = idx[j];
+        if (r < 0 || r >= dst_rows) {
+            record_status(LQ_DEV_BOUNDS);
+            continue;
+        }
+        const uint4 v = src[i];
+        const int64_t off = int64_t(r) * pieces_row + c;
+#pragma unroll
+        for (int d = 0; d < PEER_MAX; ++d)
+            if (d < G) reinterpret_cast<uint4*>(dst.p[d])[off] = v;
+    }
+    peer_meet(sync, G, rank);
 }
 
 size_t peer_sync_bytes() { return PEER_SYNC_BYTES; }
@@ -126,6 +163,36 @@ int peer_gather_run(const void* src, int M, int n, int col_off, int ldo, int ele
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cuda_status(cudaLaunchKernelEx(&cfg, peer_gather_kernel, sp, d, s, G, rank, M, pieces_row, ldp, offp));
+}
+
+int peer_scatter_rows_run(const void* src, const int32_t* idx, const int32_t* starts, const int32_t* experts,
+                          const int32_t* nseg, int bucket, int rows_max, int row_bytes, int dst_rows,
+                          void* const* dst, int G, int rank, void* const* sync, cudaStream_t st) {
+    if (G < 1 || G > PEER_MAX || rank < 0 || rank >= G || rows_max < 1 || row_bytes < 16 || dst_rows < 1)
+        return LQ_E_ARG;
+    if (row_bytes % 16 || reinterpret_cast<uintptr_t>(src) % 16) return LQ_E_ALIGN;
+    PeerPtrs d = {}, s = {};
+    for (int p = 0; p < G; ++p) {
+        if (!dst[p] || !sync[p] || reinterpret_cast<uintptr_t>(dst[p]) % 16 || reinterpret_cast<uintptr_t>(sync[p]) % 16)
+            return LQ_E_ARG;
+        d.p[p] = dst[p];
+        s.p[p] = sync[p];
+    }
+    const int pieces_row = row_bytes / 16;
+    int64_t blocks = (int64_t(rows_max) * pieces_row + 255) / 256;  // (the rows sent are known on the device only)
+    const int64_t cap = int64_t(device_info().sm_count) * 4;
+    if (blocks > cap) blocks = cap;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(blocks), 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, peer_scatter_rows_kernel, reinterpret_cast<const uint4*>(src), idx,
+                                          starts, experts, nseg, bucket, dst_rows, d, s, G, rank, pieces_row));
 }
 
 }  // namespace lq

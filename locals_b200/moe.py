@@ -64,6 +64,25 @@ def group(inds: torch.Tensor, E: int):
     return order, starts, experts, nseg, pos
 
 
+def group_range(inds: torch.Tensor, lo: int, count: int):
+    """The grouping of only the pairs routed to experts [lo, lo + count), under local ids 0 .. count - 1, every other
+    pair in the padding bucket ``count`` (sorted last; the grouped expert kernels skip it): one rank's share of an
+    expert-parallel layer (lq_moe_group_range)."""
+    flat = inds.reshape(-1).contiguous()
+    _check_cuda(flat)
+    P = flat.numel()
+    S = min(count + 1, P)
+    dev = inds.device
+    order = torch.empty(P, dtype=torch.int32, device=dev)
+    pos = torch.empty(P, dtype=torch.int32, device=dev)
+    starts = torch.empty(S + 1, dtype=torch.int32, device=dev)
+    experts = torch.empty(S, dtype=torch.int32, device=dev)
+    nseg = torch.empty(1, dtype=torch.int32, device=dev)
+    call("lq_moe_group_range", flat.data_ptr(), P, lo, count, order.data_ptr(), starts.data_ptr(), experts.data_ptr(),
+         nseg.data_ptr(), pos.data_ptr(), _stream())
+    return order, starts, experts, nseg, pos
+
+
 # Up to this many tokens a step, each (token, slot) pair is its own segment in pair order and the counting sort is
 # skipped (one launch less): a token's top-k experts are distinct, so every expert's weights are still read once. The
 # reference's own decode path computes each slot straight from its expert the same way (locals/moe.py:243-349).

@@ -223,16 +223,42 @@ class PeerGather:
         y_local = y_local.contiguous()
         M, Nl = y_local.shape
         N = Nl * self.G
-        key = (M, N, y_local.dtype)
-        if self._sync is None:
-            self._sync = PeerSync(y_local.device, self.group)
-        if key not in self._bufs:
-            self._bufs[key] = PeerOutputs((M, N), y_local.dtype, y_local.device, self.group)
-        y, addrs = self._bufs[key].next()
+        y, addrs = self._buffer((M, N, y_local.dtype), (M, N), y_local.dtype, y_local.device)
         dst = (ctypes.c_void_p * self.G)(*addrs)
         sync = (ctypes.c_void_p * self.G)(*self._sync.ptrs)
         _lib.call("lq_peer_gather_cols", y_local.data_ptr(), M, Nl, self.rank * Nl, N, y_local.element_size(), dst,
                   self.G, self.rank, sync, torch.cuda.current_stream().cuda_stream)
+        return y
+
+    def _buffer(self, key, shape, dtype, device):
+        if self._sync is None:
+            self._sync = PeerSync(device, self.group)
+        if key not in self._bufs:
+            self._bufs[key] = PeerOutputs(shape, dtype, device, self.group)
+        return self._bufs[key].next()
+
+    def rows(self, x_local: torch.Tensor) -> torch.Tensor:
+        """Every rank's (T, D) rows stacked in rank order (G T, D): the row all-gather, as one column block a rank."""
+        x_local = x_local.contiguous()
+        T, D = x_local.shape
+        return self(x_local.view(1, T * D)).view(self.G * T, D)
+
+    def scatter_rows(self, src: torch.Tensor, grouping, bucket: int, dst_rows: int) -> torch.Tensor:
+        """Rows of src (the grouped expert kernels' output in a lq_moe_group_range grouping's order) to row order[j]
+        of every rank's (dst_rows, D) buffer, the rows before the padding bucket only; returns this rank's buffer, which
+        then holds every rank's rows."""
+        import ctypes
+
+        from . import _lib
+
+        order, starts, experts, nseg, _ = grouping
+        R, D = src.shape
+        y, addrs = self._buffer(("rows", dst_rows, D, src.dtype), (dst_rows, D), src.dtype, src.device)
+        dst = (ctypes.c_void_p * self.G)(*addrs)
+        sync = (ctypes.c_void_p * self.G)(*self._sync.ptrs)
+        _lib.call("lq_peer_scatter_rows", src.data_ptr(), order.data_ptr(), starts.data_ptr(), experts.data_ptr(),
+                  nseg.data_ptr(), bucket, R, D * src.element_size(), dst_rows, dst, self.G, self.rank, sync,
+                  torch.cuda.current_stream().cuda_stream)
         return y
 
     def close(self) -> None:
@@ -387,6 +413,32 @@ class ExpertParallelMoE:
         self.up = tuple(_split_rows(t, G, r) for t in up)
         self.down = tuple(_split_rows(t, G, r) for t in down)
         self.ops = ops or kernel_ops()
+        # every rank on its own GPU and the library's kernels: the exchanges over peer memory (_call_peer)
+        self._pg = PeerGather(group) if (ops is None and G > 1 and torch.cuda.is_available()) else None
+
+    def _call_peer(self, x_local: torch.Tensor) -> torch.Tensor:
+        """Tokens gathered from every rank (peer stores), routed on every rank alike, this rank's experts' pairs
+        grouped (the rest in the padding bucket) and computed, each pair's output row stored into every rank's
+        pair-ordered buffer, and this rank's tokens combined from it -- the same kernels on the same expert segments as
+        one GPU running the whole layer, so the same bits."""
+        from . import moe
+
+        T_l, D = x_local.shape
+        G, k, EL = self.G, self.k, self.EL
+        xa = self._pg.rows(x_local)  # (G T_l, D), rank order
+        T = G * T_l
+        inds, wts = moe.route(xa, self.router_w, k, self.mode)
+        grouping = moe.group_range(inds, self.rank * EL, EL)
+        I = self.gate[0].shape[1]
+        if T <= moe.GATHER_IN_KERNEL_MAX_ROWS:
+            h = moe.experts(xa, grouping, [self.gate, self.up], I, max_rows=T, bits=self.bits, gather_k=k)
+        else:
+            h = moe.experts(moe.gather(xa, grouping[0], k), grouping, [self.gate, self.up], I, max_rows=T,
+                            bits=self.bits)
+        ys = moe.experts(h, grouping, [self.down], D, max_rows=T, bits=self.bits)  # (T k, D), grouping order
+        ys_all = self._pg.scatter_rows(ys, grouping, EL, T * k)                   # (T k, D), pair order
+        mine = slice(self.rank * T_l * k, (self.rank + 1) * T_l * k)
+        return moe.combine(ys_all[mine], wts[self.rank * T_l:(self.rank + 1) * T_l].contiguous(), None)
 
     def _a2a(self, t: torch.Tensor) -> torch.Tensor:
         if self.G == 1:
@@ -397,6 +449,9 @@ class ExpertParallelMoE:
 
     def __call__(self, x_local: torch.Tensor) -> torch.Tensor:
         """x_local: this rank's tokens (T, D) -> their MoE outputs (T, D)."""
+        if (self._pg is not None and self._pg.ok and x_local.is_cuda and self.bits == 4
+                and (x_local.shape[0] * x_local.shape[1] * x_local.element_size()) % 16 == 0):
+            return self._call_peer(x_local.contiguous())
         T, D = x_local.shape
         k, G, EL = self.k, self.G, self.EL
         inds, wts = self.ops.route(x_local, self.router_w, k, self.mode)

@@ -93,9 +93,20 @@ def _worker(rank, world, port, path):
         xt = torch.randn((2 * 8, D), generator=gen, device=dev).to(torch.bfloat16)
         full = moe.MoELayer(wr, gate, up, down, top_k=4)(xt)
         mine = xt[rank * 8:(rank + 1) * 8].contiguous()
-        got = ExpertParallelMoE(wr, gate, up, down, top_k=4)(mine)
+        ep = ExpertParallelMoE(wr, gate, up, down, top_k=4)
+        assert ep._pg is not None and ep._pg.ok  # the peer-memory exchanges (every rank on its own GPU)
         ref = full[rank * 8:(rank + 1) * 8]
+        for _ in range(3):  # (the peer buffers in turn)
+            got = ep(mine)
+            # the same kernels on the same expert segments as the one-GPU layer: the same bits
+            errs["moe_not_exact"] = max(errs.get("moe_not_exact", 0.0), float(not torch.equal(got, ref)))
         errs["moe"] = float((got.float() - ref.float()).abs().max() / ref.float().abs().max())
+        xt2 = torch.randn((2 * 40, D), generator=gen, device=dev).to(torch.bfloat16)  # 80 tokens: the gather path
+        full2 = moe.MoELayer(wr, gate, up, down, top_k=4)(xt2)
+        got2 = ep(xt2[rank * 40:(rank + 1) * 40].contiguous())
+        errs["moe80"] = float((got2.float() - full2[rank * 40:(rank + 1) * 40].float()).abs().max()
+                              / full2.float().abs().max())
+        ep._pg.close()
         torch.cuda.synchronize()
         errs["status"] = kernels.device_status()
         out = [None] * world
@@ -116,5 +127,6 @@ def test_sharded_two_gpus(tmp_path):
     for errs in torch.load(path):
         assert errs.pop("status") == 0
         assert errs.pop("peer_gather_mismatches") == 0
+        assert errs.pop("moe_not_exact") == 0
         for name, e in errs.items():
             assert e <= 1e-2, (name, e)
