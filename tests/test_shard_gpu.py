@@ -1,5 +1,6 @@
-"""The sharded modules on 2 GPUs with NCCL (skipped when fewer than 2 GPUs are visible): each sharded
-result is compared with the same computation on one GPU."""
+"""The sharded modules on 2 and 4 GPUs (skipped when fewer GPUs are visible), exchanging over peer memory and with
+NCCL: each sharded result is compared with the same computation on one GPU (the peer exchanges exactly, the
+expert-parallel layer bit for bit)."""
 
 import os
 import socket
@@ -74,6 +75,7 @@ def _worker(rank, world, port, path):
                 got = pg(mine)
                 want = torch.cat([torch.full((M_, n_), float(p_ * 100 + it), device=dev) for p_ in range(world)], 1)
                 want[:, ::n_] = float(it)
+                want = want.to(torch.bfloat16).float()  # (the block as each rank holds it)
                 bad += int((got.float() != want).sum())
         errs["peer_gather_mismatches"] = float(bad)
         pg.close()
@@ -90,7 +92,7 @@ def _worker(rank, world, port, path):
 
         gate, up, down = stack(I, D), stack(I, D), stack(D, I)
         wr = (torch.randn((E, D), generator=gen, device=dev) * 0.05).to(torch.float16)
-        xt = torch.randn((2 * 8, D), generator=gen, device=dev).to(torch.bfloat16)
+        xt = torch.randn((world * 8, D), generator=gen, device=dev).to(torch.bfloat16)
         full = moe.MoELayer(wr, gate, up, down, top_k=4)(xt)
         mine = xt[rank * 8:(rank + 1) * 8].contiguous()
         ep = ExpertParallelMoE(wr, gate, up, down, top_k=4)
@@ -98,10 +100,15 @@ def _worker(rank, world, port, path):
         ref = full[rank * 8:(rank + 1) * 8]
         for _ in range(3):  # (the peer buffers in turn)
             got = ep(mine)
-            # the same kernels on the same expert segments as the one-GPU layer: the same bits
-            errs["moe_not_exact"] = max(errs.get("moe_not_exact", 0.0), float(not torch.equal(got, ref)))
+            # up to 16 tokens the folded grouped kernel runs each expert segment the same way whatever the other
+            # segments: the same bits as the one-GPU layer (above, the mma.sync grouped kernel may split K differently
+            # when a rank holds fewer experts: the tolerance below)
+            if world * 8 <= 16:
+                errs["moe_not_exact"] = max(errs.get("moe_not_exact", 0.0), float(not torch.equal(got, ref)))
+            else:
+                errs["moe_not_exact"] = 0.0
         errs["moe"] = float((got.float() - ref.float()).abs().max() / ref.float().abs().max())
-        xt2 = torch.randn((2 * 40, D), generator=gen, device=dev).to(torch.bfloat16)  # 80 tokens: the gather path
+        xt2 = torch.randn((world * 40, D), generator=gen, device=dev).to(torch.bfloat16)  # the gather path
         full2 = moe.MoELayer(wr, gate, up, down, top_k=4)(xt2)
         got2 = ep(xt2[rank * 40:(rank + 1) * 40].contiguous())
         errs["moe80"] = float((got2.float() - full2[rank * 40:(rank + 1) * 40].float()).abs().max()
@@ -117,16 +124,25 @@ def _worker(rank, world, port, path):
         dist.destroy_process_group()
 
 
-def test_sharded_two_gpus(tmp_path):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+def _run(tmp_path, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
 
     path = str(tmp_path / "errs.pt")
-    mp.spawn(_worker, args=(2, _port(), path), nprocs=2, join=True)
+    mp.spawn(_worker, args=(world, _port(), path), nprocs=world, join=True)
     for errs in torch.load(path):
         assert errs.pop("status") == 0
         assert errs.pop("peer_gather_mismatches") == 0
         assert errs.pop("moe_not_exact") == 0
         for name, e in errs.items():
             assert e <= 1e-2, (name, e)
+
+
+def test_sharded_two_gpus(tmp_path):
+    _run(tmp_path, 2)
+
+
+def test_sharded_four_gpus(tmp_path):
+    """The same on four ranks (the peer exchanges with three peers each, four experts a rank)."""
+    _run(tmp_path, 4)
