@@ -505,25 +505,22 @@ struct MdPlan {
     size_t smem, work;
 };
 
-// Clusters of the kernel resident at once with `smem` bytes a CTA (cached per shared-memory size).
+// Clusters of the kernel resident at once with `smem` bytes a CTA on the current device (cached per device and
+// shared-memory size).
 static int md_max_clusters(size_t smem) {
     static std::mutex mu;
-    static size_t seen_smem[16];
-    static int seen_n[16];
+    static size_t seen_smem[32];
+    static int seen_dev[32], seen_n[32];
     static int nseen = 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
     std::lock_guard<std::mutex> lock(mu);
     for (int i = 0; i < nseen; ++i)
-        if (seen_smem[i] == smem) return seen_n[i];
-    static size_t attr_smem = 0;  // the kernels' dynamic shared-memory limit set so far
+        if (seen_smem[i] == smem && seen_dev[i] == dev) return seen_n[i];
     int n = 0;
-    bool ok = true;
-    if (smem > attr_smem) {
-        ok = cudaFuncSetAttribute(moe_decode_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  int(smem)) == cudaSuccess &&
-             cudaFuncSetAttribute(moe_decode_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  int(smem)) == cudaSuccess;
-        if (ok) attr_smem = smem;
-    }
+    // (the limit is a property of the current device; every launch sets it again for its own device)
+    const bool ok = cudaFuncSetAttribute(moe_decode_kernel<__nv_bfloat16>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) == cudaSuccess;
     if (ok) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(MD_CS, 1, 1);
@@ -539,8 +536,9 @@ static int md_max_clusters(size_t smem) {
         if (cudaOccupancyMaxActiveClusters(&n, moe_decode_kernel<__nv_bfloat16>, &cfg) != cudaSuccess) n = 0;
     }
     cudaGetLastError();
-    if (nseen < 16) {
+    if (nseen < 32) {
         seen_smem[nseen] = smem;
+        seen_dev[nseen] = dev;
         seen_n[nseen++] = n;
     }
     return n;
@@ -592,6 +590,10 @@ bool moe_decode_ok(int E, int k, int D, int I) {
 
 template <typename T>
 static int md_launch(const CUtensorMap& tm, const MdArgs& a, const MdPlan& p, cudaStream_t st) {
+    // set on every launch: the limit belongs to the device current at the call (as the other families do)
+    if (cudaFuncSetAttribute(moe_decode_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(p.smem)) !=
+        cudaSuccess)
+        return LQ_E_CUDA;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(MD_CS, unsigned(p.C), unsigned(a.k));
     cfg.blockDim = dim3(MD_THREADS, 1, 1);

@@ -137,3 +137,24 @@ def test_fused_decode_declines_outside_its_shapes(cuda):
     gate, up, down, wr, x = _layer(torch, 8, 192, 128, torch.bfloat16, 3, cuda)
     assert moe.decode(x, wr, gate, up, down, 2) is None
     assert moe.decode(x, wr, gate, up, down, 2, bits=8) is None
+
+
+def test_fused_decode_on_a_second_device(cuda):
+    """The kernel's shared-memory limit belongs to the device it was set on: a process that decodes on GPU 0 and then on
+    GPU 1 gets the same answers on both (skipped with one GPU)."""
+    import torch
+    from locals_b200 import moe
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    E, D, I, k = 64, 2048, 768, 4
+    ys = []
+    for d in (0, 1):
+        dev = torch.device("cuda", d)
+        with torch.cuda.device(dev):
+            gate, up, down, wr, x = _layer(torch, E, D, I, torch.bfloat16, 31, dev)
+            y = moe.decode(x, wr, gate, up, down, k)
+            torch.cuda.synchronize()
+            assert y is not None
+            ys.append(y.cpu())
+    assert torch.equal(ys[0], ys[1])
